@@ -1,0 +1,417 @@
+"""Benchmark of the fused attention layer core on B200 (one JSON line on rank 0).
+
+Workload (default): LLaMA-3-8B-shaped attention layer, bf16, B=4, H=32,
+S=8192, D=128, causal, RoPE (theta 500000) on Q and K before attention.
+One step = RoPE(Q), RoPE(K), attention forward, attention backward,
+RoPE backward of dQ and dK; with N GPUs the heads are sharded (H/N per rank)
+and the per-rank output shards are all-gathered over NCCL and reassembled
+into [B, S, H, D] (the merged-heads layout) on every rank.
+
+Metric: attention fwd+bwd TFLOP/s, FlashAttention convention
+(fwd 4*B*H*S^2*D, bwd 2.5x fwd, causal halves both: 7*B*H*S^2*D), whole job.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl haelixe|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "attn fwd+bwd TFLOP/s and % of BF16 tensor peak at 1/2/4/8 B200 vs host-CPU ref"
+UNIT = "TFLOP/s"
+# Peak used for roofline.frac: the pool's measured cuBLAS bf16 figures.
+FALLBACK_PEAK_TFLOPS = 1590.0
+# DRAM bytes per launch of the dominant kernel from one ncu capture of the
+# same command (profiles/ summary named for the kernel); None until captured.
+DOMINANT_KERNEL_TRAFFIC_BYTES = None
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["haelixe", "reference"], default="haelixe")
+    p.add_argument("--batch", type=int, default=4)
+    p.add_argument("--heads", type=int, default=32)
+    p.add_argument("--seq", type=int, default=8192)
+    p.add_argument("--head-dim", type=int, default=128)
+    p.add_argument("--no-causal", action="store_true")
+    p.add_argument("--rope-theta", type=float, default=500000.0)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def attn_flops(B, H, S, D, causal):
+    f = 14.0 * B * H * S * S * D  # fwd 4 + bwd 10
+    return f * 0.5 if causal else f
+
+
+def workload_name(a):
+    return (f"attention layer core B{a.batch} H{a.heads} S{a.seq} D{a.head_dim} "
+            f"{'causal' if not a.no_causal else 'full'} bf16, RoPE theta {a.rope_theta:g} on Q/K")
+
+
+def config_of(a, n):
+    op_mb = a.batch * a.heads * a.seq * a.head_dim * 2 / 1e6
+    return {
+        "workload": workload_name(a),
+        "batch": a.batch, "heads": a.heads, "seq_len": a.seq, "head_dim": a.head_dim,
+        "causal": not a.no_causal, "rope_theta": a.rope_theta,
+        "parallelism": f"heads/{n} per GPU + NCCL all-gather of O" if n > 1 else "1 GPU, all heads",
+        "l2": ("inputs larger than L2 (each operand %.0f MB > 126 MB)" if op_mb > 126 else
+               "inputs smaller than L2 (each operand %.0f MB); no L2 flush") % op_mb,
+        "seed": a.seed,
+    }
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(q, k, v, do, scale, causal, budget_s=12.0, max_slices=4):
+    """Oracle (C restatement of the reference's CPU path) on whole (b,h) slices."""
+    from oracle import oracle as ora
+    B, H, S, D = q.shape
+    n, t_total = 0, 0.0
+    while n < max_slices and (t_total < budget_s or n == 0):
+        b, h = n % B, (n * 7) % H
+        sl = [t[b, h].float().cpu().numpy()[None] for t in (q, k, v, do)]
+        t0 = time.perf_counter()
+        ora.attn_fwd(*sl[:3], scale, causal)
+        ora.attn_bwd(*sl, scale, causal)
+        t_total += time.perf_counter() - t0
+        n += 1
+    flops = attn_flops(1, 1, S, D, causal) * n
+    return {"value": flops / t_total / 1e12, "unit": UNIT, "cores": ora.num_threads(),
+            "kind": "port",
+            "sample": f"{n} of {B * H} (b,h) slices (S={S}, D={D}), fwd+bwd with S x S "
+                      f"matrices materialised as the reference does; {t_total:.1f} s"}
+
+
+def run_reference(a):
+    """Reference arm: the reference's CPU attention path (C restatement) on host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+    from oracle import oracle as ora
+    ora.build()
+    causal = not a.no_causal
+    S, D = a.seq, a.head_dim
+    scale = 1.0 / math.sqrt(D)
+    rng = np.random.default_rng(a.seed)
+    sl = [ora.round_bf16(rng.standard_normal((1, S, D), dtype=np.float32)) for _ in range(4)]
+    sl[0] = ora.rope_fwd(sl[0], a.rope_theta)
+    sl[1] = ora.rope_fwd(sl[1], a.rope_theta)
+
+    def step():
+        ora.attn_fwd(*sl[:3], scale, causal)
+        g = ora.attn_bwd(*sl, scale, causal)
+        ora.rope_bwd(g[0], a.rope_theta)
+        ora.rope_bwd(g[1], a.rope_theta)
+
+    for _ in range(a.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        step()
+    dt = (time.perf_counter() - t0) / a.steps
+    value = attn_flops(1, 1, S, D, causal) / dt / 1e12
+    out = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1), bf16-rounded)", "config": config_of(a, 1),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": ora.num_threads(),
+                         "kind": "port",
+                         "sample": f"one (b,h) slice (S={S}, D={D}) per step: RoPE, fwd+bwd with "
+                                   "S x S matrices materialised, RoPE bwd"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference is Rust+wgpu and cannot be built or run here; this arm times the "
+                "C restatement of its CPU kernels (oracle/) on all host cores",
+    }
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def run_haelixe(a):
+    import torch
+    import torch.distributed as dist
+
+    import haelixe_b200 as hx
+    from haelixe_b200 import _native as N
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != a.gpus:
+        raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    B, H, S, D = a.batch, a.heads, a.seq, a.head_dim
+    causal = not a.no_causal
+    if H % world:
+        raise SystemExit(f"heads {H} not divisible by {world} GPUs")
+    Hl = H // world
+    scale = 1.0 / math.sqrt(D)
+    ctx = hx.context(local)
+
+    # Inputs for this rank's heads, generated from the global head index so a
+    # head's data does not depend on the GPU count.
+    def gen(which):
+        t = torch.empty(B, Hl, S, D, device=dev, dtype=torch.bfloat16)
+        for hl in range(Hl):
+            g = torch.Generator(device=dev).manual_seed(a.seed * 1000003 + which * 1009 + rank * Hl + hl)
+            t[:, hl] = torch.randn(B, S, D, device=dev, generator=g).to(torch.bfloat16)
+        return t
+
+    q, k, v, do = (gen(i) for i in range(4))
+    qr, kr = torch.empty_like(q), torch.empty_like(k)
+    o = torch.empty_like(q)
+    lse = torch.empty(B * Hl * S, device=dev, dtype=torch.float32)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+    dq0, dk0 = torch.empty_like(q), torch.empty_like(q)
+    if world > 1:
+        gathered = torch.empty(world * B * Hl * S * D, device=dev, dtype=torch.bfloat16)
+        merged = torch.empty(B, S, H, D, device=dev, dtype=torch.bfloat16)
+        comm = torch.cuda.Stream(device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = {}
+
+    def step(timed=False):
+        if timed:
+            ev.setdefault("f0", []).append(torch.cuda.Event(enable_timing=True))
+            ev.setdefault("f1", []).append(torch.cuda.Event(enable_timing=True))
+            ev.setdefault("b1", []).append(torch.cuda.Event(enable_timing=True))
+        hx.rope_forward(q, a.rope_theta, out=qr)
+        hx.rope_forward(k, a.rope_theta, out=kr)
+        if timed:
+            ev["f0"][-1].record(stream)
+        hx.attn_forward(qr, kr, v, scale, causal, out=o, lse=lse)
+        if timed:
+            ev["f1"][-1].record(stream)
+        if world > 1:
+            done = torch.cuda.Event()
+            done.record(stream)
+            comm.wait_event(done)
+            with torch.cuda.stream(comm):
+                dist.all_gather_into_tensor(gathered, o.reshape(-1))
+        hx.attn_backward(qr, kr, v, o, lse, do, scale, causal, dq=dq, dk=dk, dv=dv)
+        if timed:
+            ev["b1"][-1].record(stream)
+        hx.rope_backward(dq, a.rope_theta, out=dq0)
+        hx.rope_backward(dk, a.rope_theta, out=dk0)
+        if world > 1:
+            stream.wait_stream(comm)
+            N.check(N.lib().hx_reassemble_heads(ctx.handle, N.HX_BF16, gathered.data_ptr(),
+                                                merged.data_ptr(), world, B, Hl, S, D, 1),
+                    ctx.handle)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    launches0 = N.lib().hx_kernel_launches(ctx.handle)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_start.record(stream)
+    for _ in range(a.steps):
+        step(timed=True)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    launches = N.lib().hx_kernel_launches(ctx.handle) - launches0
+    ms = t_start.elapsed_time(t_end) / a.steps
+    fwd_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(ev["f0"], ev["f1"]))
+    bwd_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(ev["f1"], ev["b1"]))
+    t = torch.tensor([ms, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, fwd_ms, bwd_ms = t.tolist()
+    total_flops = attn_flops(B, H, S, D, causal)
+    value = total_flops / (ms * 1e-3) / 1e12
+
+    # End to end through the C ABI with host buffers: H2D of q, k, v, dO
+    # from pinned memory, the step, D2H of o, dq, dk, dv every step.
+    e2e = None
+    if not a.no_e2e:
+        e2e = e2e_measure(a, ctx, hx, N, torch, dev, world, (q, k, v, do), (o, dq0, dk0, dv),
+                          step, total_flops)
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = cpu_baseline(qr, kr, v, do, scale, causal)
+
+    peaks = measured_peaks()
+    if peaks and peaks.get("bf16_tflops_sustained"):
+        peak, peak_src = float(peaks["bf16_tflops_sustained"]), "measured (cuBLAS bf16, sustained)"
+    else:
+        peak, peak_src = FALLBACK_PEAK_TFLOPS, "fallback"
+    dom = "bwd" if bwd_ms >= fwd_ms else "fwd"
+    dom_flops = (10.0 if dom == "bwd" else 4.0) * B * Hl * S * S * D * (0.5 if causal else 1.0)
+    dom_ms = bwd_ms if dom == "bwd" else fwd_ms
+    achieved = dom_flops / (dom_ms * 1e-3) / 1e12
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+            "config": config_of(a, world),
+            "roofline": {"bound": "tensor", "kernel": f"attention {dom} ({ctx.last_path})",
+                         "achieved": achieved, "peak": peak, "peak_source": peak_src,
+                         "unit": "TFLOP/s", "frac": achieved / peak,
+                         "traffic": DOMINANT_KERNEL_TRAFFIC_BYTES},
+            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+            "fraction_of_peak": value / world / peak,
+            "gpu_launches": int(launches),
+            "kernel_path": ctx.last_path,
+            "clocks": clocks,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def e2e_measure(a, ctx, hx, N, torch, dev, world, inputs, outputs, step, total_flops):
+    """Same step with its inputs copied in from pinned host memory and its
+    results copied back out every step, through hx_copy_*_async."""
+    import ctypes
+    steps = max(1, min(a.e2e_steps, a.steps))
+    h_in = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in inputs]
+    h_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outputs]
+    for h, t in zip(h_in, inputs):
+        h.copy_(t)
+    stream = torch.cuda.current_stream(dev)
+    ctx.use_stream(stream)
+    bi = sum(t.numel() * t.element_size() for t in inputs)
+    bo = sum(t.numel() * t.element_size() for t in outputs)
+
+    def run():
+        for h, t in zip(h_in, inputs):
+            N.check(N.lib().hx_copy_h2d_async(ctx.handle, ctypes.c_void_p(t.data_ptr()),
+                                              ctypes.c_void_p(h.data_ptr()),
+                                              t.numel() * t.element_size()), ctx.handle)
+        step()
+        ctx.use_stream(stream)
+        for h, t in zip(h_out, outputs):
+            N.check(N.lib().hx_copy_d2h_async(ctx.handle, ctypes.c_void_p(h.data_ptr()),
+                                              ctypes.c_void_p(t.data_ptr()),
+                                              t.numel() * t.element_size()), ctx.handle)
+
+    run()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(steps):
+        run()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / steps
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = t.item()
+    return {"value": total_flops / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
+            "steps": steps, "h2d_bytes_per_step": int(bi), "d2h_bytes_per_step": int(bo)}
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return run_reference(a)
+    return run_haelixe(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

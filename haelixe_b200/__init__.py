@@ -1,0 +1,19 @@
+"""haelixe_b200: B200-native (sm_100a) fused attention for the haelixe crate.
+
+The product is libhaelixe_cuda.so (C ABI: include/haelixe_cuda.h). This
+package holds its build recipe (build.py), the ctypes binding (_native.py)
+and a host-side mirror of haelixe's attention interface (attention.py).
+"""
+from .attention import (  # noqa: F401
+    CudaAllocation,
+    CudaContext,
+    FlashAttentionOp,
+    attn_backward,
+    attn_forward,
+    bin_size,
+    context,
+    flash_attention,
+    rope_backward,
+    rope_forward,
+)
+from ._native import HxError  # noqa: F401

@@ -1,0 +1,249 @@
+"""Host-side mirror of haelixe's attention interface over the C ABI.
+
+Reference interface mirrored (paths inside sethigris/haelixe):
+  * `Tensor::flash_attention(&self, k, v, scale) -> Tensor` (src/tensor.rs:644-666)
+    -> `flash_attention(q, k, v, scale, causal=False)`; like the reference it
+    attaches a `FlashAttentionOp` autograd node when q requires grad.
+  * `FlashAttentionOp { q, k, v, scale }` with `name() == "FlashAttention"` and
+    `backward(grad_out) -> [dQ, dK, dV]` (src/ops/flash_attention.rs:3-40); the
+    CUDA variant also keeps `o` and `lse`, so the backward recomputes P from
+    the saved statistics instead of re-running softmax.
+  * `Device::Cuda` / `GpuContext` (src/device.rs:5-26, src/gpu/mod.rs:38) ->
+    `CudaContext`; `GpuMemoryArena` / `GpuAllocation` (src/gpu/arena.rs) ->
+    `CudaContext.allocate()` / `CudaAllocation` (slab returns to its bin when
+    the last Python reference drops, the Arc rule of arena.rs:113-131).
+  * `rope_forward` / `rope_backward` (src/kernels/rope.rs:5-82).
+
+Device memory is held in torch CUDA tensors (plumbing only); every byte of
+compute runs in libhaelixe_cuda.so. Errors raise `HxError` (the reference
+panics).
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from typing import Optional
+
+import torch
+
+from . import _native as N
+
+_DTYPES = {torch.float32: N.HX_F32, torch.bfloat16: N.HX_BF16}
+
+
+class CudaAllocation:
+    """A binned slab from the context's arena; returned to its bin on drop."""
+
+    def __init__(self, ctx: "CudaContext", nbytes: int):
+        self._ctx = ctx
+        p = ctypes.c_void_p()
+        N.check(N.lib().hx_alloc(ctx.handle, nbytes, ctypes.byref(p)), ctx.handle)
+        self.ptr = p.value
+        self.size = int(N.lib().hx_bin_size(nbytes))
+
+    def __del__(self):
+        ctx = getattr(self, "_ctx", None)
+        if ctx is not None and ctx.handle and self.ptr:
+            N.lib().hx_free(ctx.handle, self.ptr)
+            self.ptr = None
+
+
+class CudaContext:
+    """One per device: stream, binning arena, device status word."""
+
+    def __init__(self, device: int = 0):
+        self.device = int(device)
+        h = ctypes.c_void_p()
+        st = N.lib().hx_ctx_create(self.device, ctypes.byref(h))
+        N.check(st)
+        self.handle = h.value
+
+    def close(self) -> None:
+        if self.handle:
+            N.lib().hx_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def use_stream(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        N.check(N.lib().hx_ctx_set_stream(self.handle, ctypes.c_void_p(s.cuda_stream)), self.handle)
+
+    def sync(self) -> None:
+        N.check(N.lib().hx_sync(self.handle), self.handle)
+
+    def allocate(self, nbytes: int) -> CudaAllocation:
+        return CudaAllocation(self, nbytes)
+
+    def arena_stats(self) -> dict:
+        s = N.ArenaStats()
+        N.check(N.lib().hx_arena_stats_get(self.handle, ctypes.byref(s)), self.handle)
+        return {f: int(getattr(s, f)) for f, _ in N.ArenaStats._fields_}
+
+    def arena_reset(self) -> None:
+        N.check(N.lib().hx_arena_reset(self.handle), self.handle)
+
+    @property
+    def last_path(self) -> str:
+        return {0: "none", 1: "simt", 2: "tcgen05"}[N.lib().hx_last_path(self.handle)]
+
+    def force_simt(self, on: bool) -> None:
+        N.check(N.lib().hx_set_force_simt(self.handle, int(bool(on))), self.handle)
+
+
+_ctx_lock = threading.Lock()
+_contexts: dict[int, CudaContext] = {}
+
+
+def context(device: Optional[int] = None) -> CudaContext:
+    """The cached context of `device` (default: torch's current device)."""
+    dev = torch.cuda.current_device() if device is None else int(device)
+    with _ctx_lock:
+        c = _contexts.get(dev)
+        if c is None:
+            c = CudaContext(dev)
+            _contexts[dev] = c
+    return c
+
+
+def bin_size(nbytes: int) -> int:
+    return int(N.lib().hx_bin_size(nbytes))
+
+
+def _shape_of(t: torch.Tensor) -> N.AttnShape:
+    """[BH,S,D] or [B,H,S,D] (last dim contiguous) -> hx_attn_shape."""
+    if t.dim() == 3:
+        BH, S, D = t.shape
+        sb, ss = t.stride(0), t.stride(1)
+        return N.AttnShape(BH, 1, S, D, sb, sb, ss)
+    if t.dim() == 4:
+        B, H, S, D = t.shape
+        return N.AttnShape(B, H, S, D, t.stride(0), t.stride(1), t.stride(2))
+    raise ValueError(f"attention operands are [BH,S,D] or [B,H,S,D], got {tuple(t.shape)}")
+
+
+def _check_operands(*ts: torch.Tensor) -> None:
+    t0 = ts[0]
+    for t in ts:
+        if not t.is_cuda:
+            # The reference panics here too: "FlashAttention currently requires GPU" (tensor.rs:652).
+            raise RuntimeError("FlashAttention requires CUDA tensors")
+        if t.dtype not in _DTYPES:
+            raise TypeError(f"unsupported dtype {t.dtype}; f32 and bf16 are supported")
+        if t.dtype != t0.dtype or t.shape != t0.shape or t.device != t0.device:
+            raise ValueError("q, k, v (and gradients) must share dtype, shape and device")
+        if t.stride(-1) != 1:
+            raise ValueError("the head dimension must be contiguous")
+        if t.dim() == 4 and (t.stride() != t0.stride()):
+            raise ValueError("strided operands must share strides")
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def attn_forward(q, k, v, scale: float, causal: bool = False, out=None, lse=None):
+    """Runs the fused forward. Returns (o, lse[B*H*S] f32)."""
+    _check_operands(q, k, v)
+    ctx = context(q.device.index)
+    ctx.use_stream()
+    shp = _shape_of(q)
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty(shp.B * shp.H * shp.S, device=q.device, dtype=torch.float32)
+    N.check(N.lib().hx_attn_fwd_strided(ctx.handle, _DTYPES[q.dtype], ctypes.byref(shp),
+                                        _ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(lse),
+                                        float(scale), int(bool(causal))), ctx.handle)
+    return out, lse
+
+
+def attn_backward(q, k, v, o, lse, dout, scale: float, causal: bool = False,
+                  dq=None, dk=None, dv=None):
+    """Runs the fused backward. Returns (dq, dk, dv)."""
+    dout = dout if dout.stride() == q.stride() else dout.contiguous()
+    _check_operands(q, k, v, o, dout)
+    ctx = context(q.device.index)
+    ctx.use_stream()
+    shp = _shape_of(q)
+    dq = torch.empty_like(q) if dq is None else dq
+    dk = torch.empty_like(q) if dk is None else dk
+    dv = torch.empty_like(q) if dv is None else dv
+    N.check(N.lib().hx_attn_bwd_strided(ctx.handle, _DTYPES[q.dtype], ctypes.byref(shp),
+                                        _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dout),
+                                        _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv), None, 0,
+                                        float(scale), int(bool(causal))), ctx.handle)
+    return dq, dk, dv
+
+
+class FlashAttentionOp:
+    """Autograd node of the fused attention (src/ops/flash_attention.rs:3-40)."""
+
+    def __init__(self, q, k, v, scale: float, o, lse, causal: bool = False):
+        self.q, self.k, self.v, self.scale = q, k, v, float(scale)
+        self.o, self.lse, self.causal = o, lse, bool(causal)
+
+    def name(self) -> str:
+        return "FlashAttention"
+
+    def backward(self, grad_out: torch.Tensor) -> list:
+        """Gradients for the parents in the order [q, k, v] (ops/flash_attention.rs:38)."""
+        dq, dk, dv = attn_backward(self.q, self.k, self.v, self.o, self.lse, grad_out,
+                                   self.scale, self.causal)
+        return [dq, dk, dv]
+
+
+class _FlashAttentionFn(torch.autograd.Function):
+    @staticmethod
+    def forward(fctx, q, k, v, scale, causal):
+        o, lse = attn_forward(q.detach(), k.detach(), v.detach(), scale, causal)
+        fctx.op = FlashAttentionOp(q.detach(), k.detach(), v.detach(), scale, o, lse, causal)
+        return o
+
+    @staticmethod
+    def backward(fctx, grad_out):
+        dq, dk, dv = fctx.op.backward(grad_out)
+        return dq, dk, dv, None, None
+
+
+def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+                    causal: bool = False) -> torch.Tensor:
+    """softmax(scale * q k^T [causal]) v on CUDA (Tensor::flash_attention, tensor.rs:644).
+
+    q, k, v: [B*H, S, D] (the reference's layout) or [B, H, S, D] views with a
+    contiguous head dim; f32 or bf16. When any input requires grad, the result
+    carries a FlashAttentionOp node, as `with_node` does in the reference
+    (tensor.rs:655-663).
+    """
+    if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
+        return _FlashAttentionFn.apply(q, k, v, float(scale), bool(causal))
+    o, _ = attn_forward(q, k, v, scale, causal)
+    return o
+
+
+def rope_forward(x: torch.Tensor, base: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Interleaved-pair RoPE on [BH,S,D] / [B,H,S,D] (kernels/rope.rs:5-44)."""
+    _check_operands(x)
+    ctx = context(x.device.index)
+    ctx.use_stream()
+    out = torch.empty_like(x) if out is None else out
+    shp = _shape_of(x)
+    N.check(N.lib().hx_rope_fwd(ctx.handle, _DTYPES[x.dtype], ctypes.byref(shp), _ptr(x),
+                                _ptr(out), float(base)), ctx.handle)
+    return out
+
+
+def rope_backward(g: torch.Tensor, base: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Inverse rotation (kernels/rope.rs:46-82)."""
+    _check_operands(g)
+    ctx = context(g.device.index)
+    ctx.use_stream()
+    out = torch.empty_like(g) if out is None else out
+    shp = _shape_of(g)
+    N.check(N.lib().hx_rope_bwd(ctx.handle, _DTYPES[g.dtype], ctypes.byref(shp), _ptr(g),
+                                _ptr(out), float(base)), ctx.handle)
+    return out

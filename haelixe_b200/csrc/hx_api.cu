@@ -1,0 +1,525 @@
+// C ABI implementation: context, binning arena, transfers and dispatch of
+// the attention and RoPE kernels. See include/haelixe_cuda.h for the
+// reference interface each entry point replaces.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+
+#include "hx_internal.h"
+
+namespace hx {
+
+int set_error(const hx_ctx* ctx, int status, const char* fmt, ...) {
+    if (ctx != nullptr) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof(buf), fmt, ap);
+        va_end(ap);
+        std::lock_guard<std::mutex> g(ctx->err_mu);
+        const_cast<hx_ctx*>(ctx)->last_error = buf;
+    }
+    return status;
+}
+
+static thread_local uint64_t t_launches = 0;
+void note_launch() { ++t_launches; }
+uint64_t launches_of_this_thread() { return t_launches; }
+
+int check_cuda(const hx_ctx* ctx, cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return HX_OK;
+    const int st = (e == cudaErrorMemoryAllocation) ? HX_ERR_OOM : HX_ERR_CUDA;
+    return set_error(ctx, st, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+}  // namespace hx
+
+using hx::check_cuda;
+using hx::set_error;
+
+namespace {
+
+// Adds the kernels launched during one public call to the context's count.
+struct LaunchCount {
+    hx_ctx* c;
+    uint64_t t0;
+    explicit LaunchCount(hx_ctx* ctx) : c(ctx), t0(hx::launches_of_this_thread()) {}
+    ~LaunchCount() { c->kernel_launches += hx::launches_of_this_thread() - t0; }
+};
+
+// RAII guard that makes the context's device current for one call and
+// restores the caller's device afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int validate_shape(const hx_ctx* ctx, const hx_attn_shape* s, const char* who) {
+    if (s == nullptr) return set_error(ctx, HX_ERR_INVALID, "%s: shape is NULL", who);
+    if (s->B <= 0 || s->H <= 0 || s->S <= 0 || s->D <= 0)
+        return set_error(ctx, HX_ERR_INVALID, "%s: B, H, S, D must be positive (got %d,%d,%d,%d)",
+                         who, s->B, s->H, s->S, s->D);
+    if (s->D > 256)
+        return set_error(ctx, HX_ERR_UNSUPPORTED, "%s: head_dim %d > 256 is not supported", who,
+                         s->D);
+    if (s->B > 65535 || s->H > 65535)
+        return set_error(ctx, HX_ERR_UNSUPPORTED, "%s: B and H must be <= 65535", who);
+    if (s->stride_s < s->D || s->stride_h < 0 || s->stride_b < 0)
+        return set_error(ctx, HX_ERR_INVALID,
+                         "%s: strides (b=%lld, h=%lld, s=%lld) overlap rows of length D=%d", who,
+                         (long long)s->stride_b, (long long)s->stride_h, (long long)s->stride_s,
+                         s->D);
+    return HX_OK;
+}
+
+int validate_dtype(const hx_ctx* ctx, hx_dtype dt, const char* who) {
+    if (dt != HX_F32 && dt != HX_BF16)
+        return set_error(ctx, HX_ERR_INVALID, "%s: unknown dtype %d", who, (int)dt);
+    return HX_OK;
+}
+
+inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// The tcgen05 kernels move tiles with TMA: base addresses and every stride
+// must be 16-byte multiples.
+bool tma_layout_ok(const hx::AttnDims& d, std::initializer_list<const void*> ptrs) {
+    const int64_t eb = 2;  // bf16
+    if ((d.ss * eb) % 16 || (d.sh * eb) % 16 || (d.sb * eb) % 16) return false;
+    for (const void* p : ptrs)
+        if (!aligned16(p)) return false;
+    return true;
+}
+
+uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
+
+uint64_t simt_ws_bytes(const hx::AttnDims& d) {
+    return align256((uint64_t)d.B * d.H * d.S * sizeof(float));
+}
+
+}  // namespace
+
+extern "C" {
+
+int hx_abi_version(void) { return HX_ABI_VERSION; }
+
+const char* hx_status_string(int status) {
+    switch (status) {
+        case HX_OK: return "ok";
+        case HX_ERR_INVALID: return "invalid argument";
+        case HX_ERR_UNSUPPORTED: return "unsupported";
+        case HX_ERR_CUDA: return "CUDA error";
+        case HX_ERR_OOM: return "out of device memory";
+        case HX_ERR_TIMEOUT: return "device wait timed out";
+        case HX_ERR_NCCL: return "collective error";
+        default: return "unknown status";
+    }
+}
+
+int hx_ctx_create(int device, hx_ctx** out) {
+    if (out == nullptr) return HX_ERR_INVALID;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return HX_ERR_INVALID;
+    DeviceGuard g(device);
+    if (!g.ok) return HX_ERR_CUDA;
+    hx_ctx* c = new hx_ctx();
+    c->device = device;
+    int st = HX_OK;
+    do {
+        if ((st = check_cuda(c, cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount,
+                                                       device),
+                             "cudaDeviceGetAttribute")))
+            break;
+        if ((st = check_cuda(c, cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking),
+                             "cudaStreamCreateWithFlags")))
+            break;
+        c->stream = c->own_stream;
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = device;
+        if ((st = check_cuda(c, cudaMemPoolCreate(&c->arena.pool, &props), "cudaMemPoolCreate")))
+            break;
+        uint64_t threshold = UINT64_MAX;
+        if ((st = check_cuda(c, cudaMemPoolSetAttribute(c->arena.pool,
+                                                        cudaMemPoolAttrReleaseThreshold, &threshold),
+                             "cudaMemPoolSetAttribute")))
+            break;
+        if ((st = check_cuda(c, cudaMalloc(&c->status, sizeof(hx::DeviceStatus)), "cudaMalloc")))
+            break;
+        if ((st = check_cuda(c, cudaMemset(c->status, 0, sizeof(hx::DeviceStatus)), "cudaMemset")))
+            break;
+    } while (0);
+    if (st != HX_OK) {
+        hx_ctx_destroy(c);
+        return st;
+    }
+    *out = c;
+    return HX_OK;
+}
+
+int hx_ctx_destroy(hx_ctx* c) {
+    if (c == nullptr) return HX_OK;
+    DeviceGuard g(c->device);
+    if (c->own_stream) cudaStreamSynchronize(c->own_stream);
+    if (c->stream && c->stream != c->own_stream) cudaStreamSynchronize(c->stream);
+    if (c->own_stream) {
+        std::lock_guard<std::mutex> lk(c->arena.mu);
+        for (auto& kv : c->arena.free_list)
+            for (void* p : kv.second) cudaFreeAsync(p, c->own_stream);
+        for (auto& kv : c->arena.live) cudaFreeAsync(kv.first, c->own_stream);
+        c->arena.free_list.clear();
+        c->arena.live.clear();
+        cudaStreamSynchronize(c->own_stream);
+    }
+    if (c->arena.pool) cudaMemPoolDestroy(c->arena.pool);
+    if (c->status) cudaFree(c->status);
+    if (c->own_stream) cudaStreamDestroy(c->own_stream);
+    delete c;
+    return HX_OK;
+}
+
+int hx_ctx_device(const hx_ctx* c, int* device) {
+    if (c == nullptr || device == nullptr) return HX_ERR_INVALID;
+    *device = c->device;
+    return HX_OK;
+}
+
+void* hx_ctx_stream(hx_ctx* c) { return c ? (void*)c->stream : nullptr; }
+
+int hx_ctx_set_stream(hx_ctx* c, void* stream) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    c->stream = stream ? (cudaStream_t)stream : c->own_stream;
+    return HX_OK;
+}
+
+int hx_sync(hx_ctx* c) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    DeviceGuard g(c->device);
+    int st = check_cuda(c, cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+    if (st != HX_OK) return st;
+    hx::DeviceStatus s{};
+    st = check_cuda(c, cudaMemcpy(&s, c->status, sizeof(s), cudaMemcpyDeviceToHost), "cudaMemcpy");
+    if (st != HX_OK) return st;
+    if (s.code != 0) {
+        cudaMemset(c->status, 0, sizeof(hx::DeviceStatus));
+        return set_error(c, HX_ERR_TIMEOUT,
+                         "a device-side bounded wait expired (code %d at site %d, block %d)",
+                         s.code, s.where, s.block);
+    }
+    return HX_OK;
+}
+
+int hx_last_error(const hx_ctx* c, char* buf, size_t len) {
+    if (c == nullptr || buf == nullptr || len == 0) return HX_ERR_INVALID;
+    std::lock_guard<std::mutex> g(c->err_mu);
+    snprintf(buf, len, "%s", c->last_error.c_str());
+    return HX_OK;
+}
+
+// ---- arena ------------------------------------------------------------------
+
+uint64_t hx_bin_size(uint64_t requested) {
+    const uint64_t kMin = 512;  // arena.rs:85
+    if (requested <= kMin) return kMin;
+    uint64_t b = 1;
+    while (b < requested) b <<= 1;  // next_power_of_two (arena.rs:89)
+    return b;
+}
+
+int hx_alloc(hx_ctx* c, uint64_t bytes, void** ptr) {
+    if (c == nullptr || ptr == nullptr) return HX_ERR_INVALID;
+    *ptr = nullptr;
+    const uint64_t bin = hx_bin_size(bytes);
+    {
+        std::lock_guard<std::mutex> lk(c->arena.mu);
+        auto it = c->arena.free_list.find(bin);
+        if (it != c->arena.free_list.end() && !it->second.empty()) {
+            void* p = it->second.back();
+            it->second.pop_back();
+            if (it->second.empty()) c->arena.free_list.erase(it);
+            c->arena.cached_bytes -= bin;
+            c->arena.live[p] = bin;
+            c->arena.live_bytes += bin;
+            c->arena.hits++;
+            *ptr = p;
+            return HX_OK;
+        }
+    }
+    // Miss: the mutex is released before the driver call (arena.rs:45-47).
+    DeviceGuard g(c->device);
+    void* p = nullptr;
+    cudaError_t e = cudaMallocFromPoolAsync(&p, bin, c->arena.pool, c->stream);
+    if (e == cudaErrorMemoryAllocation) {
+        cudaGetLastError();
+        hx_arena_reset(c);  // give parked slabs back, then retry once
+        e = cudaMallocFromPoolAsync(&p, bin, c->arena.pool, c->stream);
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return check_cuda(c, e, "cudaMallocFromPoolAsync");
+    }
+    std::lock_guard<std::mutex> lk(c->arena.mu);
+    c->arena.live[p] = bin;
+    c->arena.live_bytes += bin;
+    c->arena.misses++;
+    *ptr = p;
+    return HX_OK;
+}
+
+int hx_free(hx_ctx* c, void* ptr) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    if (ptr == nullptr) return HX_OK;
+    std::lock_guard<std::mutex> lk(c->arena.mu);
+    auto it = c->arena.live.find(ptr);
+    if (it == c->arena.live.end())
+        return set_error(c, HX_ERR_INVALID, "hx_free: %p was not allocated by this arena", ptr);
+    const uint64_t bin = it->second;
+    c->arena.live.erase(it);
+    c->arena.live_bytes -= bin;
+    c->arena.free_list[bin].push_back(ptr);
+    c->arena.cached_bytes += bin;
+    return HX_OK;
+}
+
+int hx_arena_reset(hx_ctx* c) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    DeviceGuard g(c->device);
+    std::lock_guard<std::mutex> lk(c->arena.mu);
+    for (auto& kv : c->arena.free_list)
+        for (void* p : kv.second) cudaFreeAsync(p, c->stream);
+    c->arena.free_list.clear();
+    c->arena.cached_bytes = 0;
+    return check_cuda(c, cudaGetLastError(), "cudaFreeAsync");
+}
+
+int hx_arena_stats_get(const hx_ctx* c, hx_arena_stats* out) {
+    if (c == nullptr || out == nullptr) return HX_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(const_cast<hx_ctx*>(c)->arena.mu);
+    out->live_bytes = c->arena.live_bytes;
+    out->cached_bytes = c->arena.cached_bytes;
+    uint64_t slabs = 0;
+    for (auto& kv : c->arena.free_list) slabs += kv.second.size();
+    out->cached_slabs = slabs;
+    out->cached_bins = c->arena.free_list.size();
+    out->hits = c->arena.hits;
+    out->misses = c->arena.misses;
+    return HX_OK;
+}
+
+// ---- transfers ----------------------------------------------------------------
+
+int hx_copy_h2d_async(hx_ctx* c, void* dst, const void* src, uint64_t bytes) {
+    if (c == nullptr || (bytes && (dst == nullptr || src == nullptr))) return HX_ERR_INVALID;
+    DeviceGuard g(c->device);
+    return check_cuda(c, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->stream),
+                      "cudaMemcpyAsync(H2D)");
+}
+
+int hx_copy_d2h_async(hx_ctx* c, void* dst, const void* src, uint64_t bytes) {
+    if (c == nullptr || (bytes && (dst == nullptr || src == nullptr))) return HX_ERR_INVALID;
+    DeviceGuard g(c->device);
+    return check_cuda(c, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, c->stream),
+                      "cudaMemcpyAsync(D2H)");
+}
+
+int hx_copy_h2d(hx_ctx* c, void* dst, const void* src, uint64_t bytes) {
+    int st = hx_copy_h2d_async(c, dst, src, bytes);
+    if (st != HX_OK) return st;
+    return check_cuda(c, cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+}
+
+int hx_copy_d2h(hx_ctx* c, void* dst, const void* src, uint64_t bytes) {
+    int st = hx_copy_d2h_async(c, dst, src, bytes);
+    if (st != HX_OK) return st;
+    return check_cuda(c, cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+}
+
+int hx_host_alloc_pinned(uint64_t bytes, void** ptr) {
+    if (ptr == nullptr) return HX_ERR_INVALID;
+    cudaError_t e = cudaMallocHost(ptr, bytes);
+    return e == cudaSuccess ? HX_OK : (e == cudaErrorMemoryAllocation ? HX_ERR_OOM : HX_ERR_CUDA);
+}
+
+int hx_host_free_pinned(void* ptr) {
+    return cudaFreeHost(ptr) == cudaSuccess ? HX_OK : HX_ERR_CUDA;
+}
+
+// ---- attention --------------------------------------------------------------------
+
+int hx_attn_fwd_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* q,
+                        const void* k, const void* v, void* o, float* lse, float scale,
+                        int causal) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, "hx_attn_fwd")) || (st = validate_shape(c, shape, "hx_attn_fwd")))
+        return st;
+    if (!q || !k || !v || !o) return set_error(c, HX_ERR_INVALID, "hx_attn_fwd: NULL operand");
+    if (!isfinite(scale)) return set_error(c, HX_ERR_INVALID, "hx_attn_fwd: scale is not finite");
+    DeviceGuard g(c->device);
+    LaunchCount lc(c);
+    const hx::AttnDims d = hx::dims_of(*shape);
+    const bool fast = !c->force_simt && lse != nullptr && hx::sm100_supported(dt, d) &&
+                      tma_layout_ok(d, {q, k, v, o});
+    cudaError_t e;
+    if (fast) {
+        e = hx::sm100_attn_fwd(c->stream, c->sm_count, c->status, d, q, k, v, o, lse, scale,
+                               causal);
+        c->last_path = 2;
+    } else {
+        e = hx::simt_attn_fwd(c->stream, dt, d, q, k, v, o, lse, scale, causal);
+        c->last_path = 1;
+    }
+    return check_cuda(c, e, fast ? "attention forward (tcgen05)" : "attention forward (SIMT)");
+}
+
+int hx_attn_bwd_workspace_size(hx_dtype dt, const hx_attn_shape* shape, uint64_t* bytes) {
+    if (shape == nullptr || bytes == nullptr) return HX_ERR_INVALID;
+    if (validate_dtype(nullptr, dt, "") || validate_shape(nullptr, shape, "")) return HX_ERR_INVALID;
+    const hx::AttnDims d = hx::dims_of(*shape);
+    uint64_t n = simt_ws_bytes(d);
+    if (hx::sm100_supported(dt, d)) n = std::max(n, hx::sm100_bwd_workspace_bytes(d));
+    *bytes = n;
+    return HX_OK;
+}
+
+int hx_attn_bwd_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* q,
+                        const void* k, const void* v, const void* o, const void* dout,
+                        const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                        uint64_t workspace_bytes, float scale, int causal) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, "hx_attn_bwd")) || (st = validate_shape(c, shape, "hx_attn_bwd")))
+        return st;
+    if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv)
+        return set_error(c, HX_ERR_INVALID, "hx_attn_bwd: NULL operand");
+    if (!isfinite(scale)) return set_error(c, HX_ERR_INVALID, "hx_attn_bwd: scale is not finite");
+    DeviceGuard g(c->device);
+    LaunchCount lc(c);
+    const hx::AttnDims d = hx::dims_of(*shape);
+    const bool fast = !c->force_simt && hx::sm100_supported(dt, d) &&
+                      tma_layout_ok(d, {q, k, v, o, dout, dq, dk, dv});
+    const uint64_t need = fast ? hx::sm100_bwd_workspace_bytes(d) : simt_ws_bytes(d);
+    void* ws = workspace;
+    bool owned = false;
+    if (ws == nullptr) {
+        if ((st = hx_alloc(c, need, &ws))) return st;
+        owned = true;
+    } else if (workspace_bytes < need) {
+        return set_error(c, HX_ERR_INVALID, "hx_attn_bwd: workspace of %llu bytes < %llu needed",
+                         (unsigned long long)workspace_bytes, (unsigned long long)need);
+    } else if (((uintptr_t)ws & 255u) != 0) {
+        return set_error(c, HX_ERR_INVALID, "hx_attn_bwd: workspace must be 256-byte aligned");
+    }
+    cudaError_t e;
+    if (fast) {
+        e = hx::sm100_attn_bwd(c->stream, c->sm_count, c->status, d, q, k, v, o, dout, lse, dq, dk,
+                               dv, ws, scale, causal);
+        c->last_path = 2;
+    } else {
+        e = hx::simt_attn_bwd(c->stream, dt, d, q, k, v, o, dout, lse, dq, dk, dv, (float*)ws,
+                              scale, causal);
+        c->last_path = 1;
+    }
+    st = check_cuda(c, e, fast ? "attention backward (tcgen05)" : "attention backward (SIMT)");
+    if (owned) hx_free(c, ws);  // stream-ordered: the next user of the slab queues behind us
+    return st;
+}
+
+static hx_attn_shape contiguous_shape(int bh, int seq_len, int head_dim) {
+    hx_attn_shape s;
+    s.B = bh;
+    s.H = 1;
+    s.S = seq_len;
+    s.D = head_dim;
+    s.stride_s = head_dim;
+    s.stride_h = (int64_t)seq_len * head_dim;
+    s.stride_b = (int64_t)seq_len * head_dim;
+    return s;
+}
+
+int hx_flash_attention_fwd(hx_ctx* c, hx_dtype dt, const void* q, const void* k, const void* v,
+                           void* o, float* lse, int bh, int seq_len, int head_dim, float scale,
+                           int causal) {
+    const hx_attn_shape s = contiguous_shape(bh, seq_len, head_dim);
+    return hx_attn_fwd_strided(c, dt, &s, q, k, v, o, lse, scale, causal);
+}
+
+int hx_flash_attention_bwd(hx_ctx* c, hx_dtype dt, const void* q, const void* k, const void* v,
+                           const void* o, const void* dout, const float* lse, void* dq, void* dk,
+                           void* dv, void* workspace, uint64_t workspace_bytes, int bh,
+                           int seq_len, int head_dim, float scale, int causal) {
+    const hx_attn_shape s = contiguous_shape(bh, seq_len, head_dim);
+    return hx_attn_bwd_strided(c, dt, &s, q, k, v, o, dout, lse, dq, dk, dv, workspace,
+                               workspace_bytes, scale, causal);
+}
+
+// ---- RoPE -----------------------------------------------------------------------------
+
+static int rope_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* x,
+                       void* out, float base, float sign, const char* who) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, who)) || (st = validate_shape(c, shape, who))) return st;
+    if (!x || !out) return set_error(c, HX_ERR_INVALID, "%s: NULL operand", who);
+    if (shape->D % 2) return set_error(c, HX_ERR_INVALID, "%s: head_dim must be even", who);
+    // base^(-(2i)/D) in f32, the reference's expression (src/kernels/rope.rs:27-28).
+    float inv_freq[128];
+    for (int i = 0; i < shape->D / 2; ++i) {
+        const float exponent = -((float)(2 * i)) / (float)shape->D;
+        inv_freq[i] = powf(base, exponent);
+    }
+    DeviceGuard g(c->device);
+    LaunchCount lc(c);
+    return check_cuda(c, hx::rope_apply(c->stream, dt, hx::dims_of(*shape), x, out, inv_freq, sign),
+                      who);
+}
+
+int hx_rope_fwd(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* x, void* out,
+                float base) {
+    return rope_common(c, dt, shape, x, out, base, 1.f, "hx_rope_fwd");
+}
+
+int hx_rope_bwd(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* g, void* out,
+                float base) {
+    return rope_common(c, dt, shape, g, out, base, -1.f, "hx_rope_bwd");
+}
+
+int hx_reassemble_heads(hx_ctx* c, hx_dtype dt, const void* shards, void* out, int n_shards,
+                        int B, int H_shard, int S, int D, int out_layout) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, "hx_reassemble_heads"))) return st;
+    if (!shards || !out || n_shards <= 0 || B <= 0 || H_shard <= 0 || S <= 0 || D <= 0 ||
+        (out_layout != 0 && out_layout != 1))
+        return set_error(c, HX_ERR_INVALID, "hx_reassemble_heads: bad arguments");
+    DeviceGuard g(c->device);
+    LaunchCount lc(c);
+    return check_cuda(c, hx::reassemble_heads(c->stream, dt == HX_F32 ? 4 : 2, shards, out,
+                                              n_shards, B, H_shard, S, D, out_layout,
+                                              c->sm_count),
+                      "hx_reassemble_heads");
+}
+
+uint64_t hx_kernel_launches(const hx_ctx* c) { return c ? c->kernel_launches : 0; }
+
+int hx_last_path(const hx_ctx* c) { return c ? c->last_path : 0; }
+
+int hx_set_force_simt(hx_ctx* c, int force) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    c->force_simt = force ? 1 : 0;
+    return HX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,97 @@
+// Internal declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/haelixe_cuda.h"
+
+namespace hx {
+
+// Device status word written by kernels whose bounded waits expire.
+// 0 = fine; otherwise a code naming the wait that gave up.
+struct DeviceStatus {
+    int code;
+    int where;
+    int block;
+    int pad;
+};
+
+struct Arena {
+    cudaMemPool_t pool = nullptr;
+    std::mutex mu;
+    std::unordered_map<uint64_t, std::vector<void*>> free_list;  // bin -> slabs
+    std::unordered_map<void*, uint64_t> live;                    // slab -> bin
+    uint64_t live_bytes = 0, cached_bytes = 0, hits = 0, misses = 0;
+};
+
+}  // namespace hx
+
+struct hx_ctx {
+    int device = 0;
+    int sm_count = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    hx::Arena arena;
+    hx::DeviceStatus* status = nullptr;  // device memory
+    int last_path = 0;
+    uint64_t kernel_launches = 0;
+    int force_simt = 0;
+    mutable std::mutex err_mu;
+    std::string last_error;
+};
+
+namespace hx {
+
+// Per-operand view: element strides, D contiguous.
+struct AttnDims {
+    int B, H, S, D;
+    int64_t sb, sh, ss;
+};
+
+inline AttnDims dims_of(const hx_attn_shape& s) {
+    return AttnDims{s.B, s.H, s.S, s.D, s.stride_b, s.stride_h, s.stride_s};
+}
+
+int set_error(const hx_ctx* ctx, int status, const char* fmt, ...);
+int check_cuda(const hx_ctx* ctx, cudaError_t e, const char* what);
+
+// ---- SIMT kernels (attn_simt.cu): any head_dim <= 256, f32 or bf16 ----
+cudaError_t simt_attn_fwd(cudaStream_t st, hx_dtype dt, const AttnDims& d, const void* q,
+                          const void* k, const void* v, void* o, float* lse, float scale,
+                          int causal);
+cudaError_t simt_attn_bwd(cudaStream_t st, hx_dtype dt, const AttnDims& d, const void* q,
+                          const void* k, const void* v, const void* o, const void* dout,
+                          const float* lse, void* dq, void* dk, void* dv, float* delta,
+                          float scale, int causal);
+
+// ---- tcgen05 kernels (attn_fwd_sm100.cu / attn_bwd_sm100.cu): bf16, D in {64,128} ----
+bool sm100_supported(hx_dtype dt, const AttnDims& d);
+cudaError_t sm100_attn_fwd(cudaStream_t st, int sm_count, DeviceStatus* status,
+                           const AttnDims& d, const void* q, const void* k, const void* v,
+                           void* o, float* lse, float scale, int causal);
+uint64_t sm100_bwd_workspace_bytes(const AttnDims& d);
+cudaError_t sm100_attn_bwd(cudaStream_t st, int sm_count, DeviceStatus* status,
+                           const AttnDims& d, const void* q, const void* k, const void* v,
+                           const void* o, const void* dout, const float* lse, void* dq,
+                           void* dk, void* dv, void* workspace, float scale, int causal);
+
+// ---- head reassembly (heads.cu) ----
+cudaError_t reassemble_heads(cudaStream_t st, int elem_bytes, const void* src, void* dst, int n,
+                             int B, int Hs, int S, int D, int layout, int sm_count);
+
+// Counts kernel launches of the calling thread; hx_api attributes them to a context.
+void note_launch();
+uint64_t launches_of_this_thread();
+
+// ---- RoPE (rope.cu) ----
+cudaError_t rope_apply(cudaStream_t st, hx_dtype dt, const AttnDims& d, const void* x, void* out,
+                       const float* inv_freq_host, float sign);
+
+}  // namespace hx

@@ -1,0 +1,186 @@
+/*
+ * haelixe_cuda.h - C ABI of the B200 (sm_100a) fused attention library.
+ *
+ * This is the boundary that haelixe's Rust crate binds through `extern "C"`
+ * (see INTEGRATION.md for the Rust declarations and the build.rs step).
+ * Plain pointers and sizes only: device pointers are raw CUDA device
+ * addresses on the context's device, host pointers are ordinary host memory.
+ *
+ * Reference interfaces replaced (paths inside sethigris/haelixe):
+ *   hx_ctx_create / hx_ctx_destroy    <- GpuContext::new (src/gpu/mod.rs:38)
+ *                                        and Device::gpu (src/device.rs:16-18)
+ *   hx_alloc / hx_free / hx_arena_*   <- GpuMemoryArena::allocate / free / reset
+ *                                        (src/gpu/arena.rs:25,64,76), and
+ *                                        GpuAllocation::drop (arena.rs:113-131)
+ *   hx_bin_size                       <- get_bin_size (src/gpu/arena.rs:84-91)
+ *   hx_copy_h2d / hx_copy_d2h         <- Tensor::to upload / download_from_gpu
+ *                                        (src/tensor.rs:300-391)
+ *   hx_flash_attention_fwd            <- GpuContext::flash_attention_gpu
+ *                                        (src/gpu/mod.rs:1336-1418), called by
+ *                                        Tensor::flash_attention (src/tensor.rs:644-666)
+ *   hx_flash_attention_bwd            <- FlashAttentionOp::backward
+ *                                        (src/ops/flash_attention.rs:16-39)
+ *   hx_attn_fwd_strided / _bwd_strided   the same two operations on strided
+ *                                        [B,H,S,D] views, replacing the
+ *                                        view/transpose/view head split of
+ *                                        MultiHeadAttention::forward
+ *                                        (src/nn/attention.rs:62-73,91-94)
+ *   hx_rope_fwd / hx_rope_bwd         <- rope_forward / rope_backward
+ *                                        (src/kernels/rope.rs:5-82)
+ *
+ * Error behaviour: every entry point returns 0 (HX_OK) or a negative
+ * hx_status. The reference panics instead (e.g. src/tensor.rs:652,
+ * src/gpu/mod.rs:45); a Rust wrapper turns a non-zero status into
+ * `panic!` with the text of hx_last_error. All work is enqueued on the
+ * context's stream and is asynchronous to the host, except the copies,
+ * hx_sync and calls that must read a device status word.
+ */
+#ifndef HAELIXE_CUDA_H
+#define HAELIXE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HX_ABI_VERSION 1
+
+typedef struct hx_ctx hx_ctx;
+
+typedef enum hx_dtype {
+    HX_F32 = 0,  /* f32 storage, f32 arithmetic (the reference's only GPU dtype) */
+    HX_BF16 = 1, /* bf16 storage, f32 accumulation (src/dtype.rs:4-13 BF16) */
+} hx_dtype;
+
+typedef enum hx_status {
+    HX_OK = 0,
+    HX_ERR_INVALID = -1,     /* null pointer, bad shape, stride or alignment */
+    HX_ERR_UNSUPPORTED = -2, /* well-formed but not supported (e.g. head_dim > 256) */
+    HX_ERR_CUDA = -3,        /* a CUDA runtime call failed */
+    HX_ERR_OOM = -4,         /* device memory exhausted */
+    HX_ERR_TIMEOUT = -5,     /* a bounded device-side wait expired; the context stays usable */
+    HX_ERR_NCCL = -6,        /* a collective failed */
+} hx_status;
+
+/* Shape and element strides of one attention operand viewed as [B, H, S, D]
+ * with D contiguous. q, k, v, o, dO, dQ, dK and dV of one call share it.
+ * The reference's contiguous [B*H, S, D] tensors are B = B*H, H = 1,
+ * stride_s = D, stride_b = S*D (what hx_flash_attention_* pass). */
+typedef struct hx_attn_shape {
+    int32_t B, H, S, D;
+    int64_t stride_b, stride_h, stride_s;
+} hx_attn_shape;
+
+typedef struct hx_arena_stats {
+    uint64_t live_bytes;   /* binned bytes handed out and not yet returned */
+    uint64_t cached_bytes; /* binned bytes parked in the free lists */
+    uint64_t cached_slabs; /* number of parked slabs */
+    uint64_t cached_bins;  /* number of distinct bin sizes with parked slabs */
+    uint64_t hits;         /* allocations served from a free list */
+    uint64_t misses;       /* allocations that went to the CUDA pool */
+} hx_arena_stats;
+
+/* ---- library / context ---------------------------------------------------- */
+int hx_abi_version(void);
+const char* hx_status_string(int status);
+
+/* Creates a context on `device`: its own non-blocking stream, a binning arena
+ * over a cudaMallocAsync pool, and a device status word for bounded waits. */
+int hx_ctx_create(int device, hx_ctx** out);
+int hx_ctx_destroy(hx_ctx* ctx);
+int hx_ctx_device(const hx_ctx* ctx, int* device);
+/* The cudaStream_t the context enqueues on (as void*). */
+void* hx_ctx_stream(hx_ctx* ctx);
+/* Replace the stream (NULL restores the context's own stream). */
+int hx_ctx_set_stream(hx_ctx* ctx, void* stream);
+/* Blocks until the stream drains; reports a pending device timeout. */
+int hx_sync(hx_ctx* ctx);
+/* Copies the last error text (NUL-terminated) into buf. */
+int hx_last_error(const hx_ctx* ctx, char* buf, size_t len);
+
+/* ---- binning arena (src/gpu/arena.rs) -------------------------------------- */
+/* Power-of-two bin with a 512-byte floor (arena.rs:84-91). */
+uint64_t hx_bin_size(uint64_t requested_bytes);
+/* Returns a slab of hx_bin_size(bytes) bytes, 256-byte aligned, stream-ordered. */
+int hx_alloc(hx_ctx* ctx, uint64_t bytes, void** ptr);
+/* Returns the slab to its bin: the caller calls this when its last reference
+ * drops (the Arc strong_count==1 rule of arena.rs:126). */
+int hx_free(hx_ctx* ctx, void* ptr);
+/* Releases every parked slab back to the CUDA pool (arena.rs:76-80). */
+int hx_arena_reset(hx_ctx* ctx);
+int hx_arena_stats_get(const hx_ctx* ctx, hx_arena_stats* out);
+
+/* ---- transfers --------------------------------------------------------------- */
+int hx_copy_h2d(hx_ctx* ctx, void* dst_dev, const void* src_host, uint64_t bytes);
+int hx_copy_d2h(hx_ctx* ctx, void* dst_host, const void* src_dev, uint64_t bytes);
+int hx_copy_h2d_async(hx_ctx* ctx, void* dst_dev, const void* src_host, uint64_t bytes);
+int hx_copy_d2h_async(hx_ctx* ctx, void* dst_host, const void* src_dev, uint64_t bytes);
+int hx_host_alloc_pinned(uint64_t bytes, void** ptr);
+int hx_host_free_pinned(void* ptr);
+
+/* ---- fused attention, contiguous [BH, S, D] (the reference's layout) -------- */
+/* o = softmax(scale * q k^T [+ causal mask]) v ; lse[BH*S] (f32, may be NULL
+ * only when no backward follows) receives the per-row log-sum-exp.
+ * Mirrors the reference's Params{bh, seq_len, head_dim, scale}
+ * (src/gpu/mod.rs:1354) plus the causal flag the reference lacks. */
+int hx_flash_attention_fwd(hx_ctx* ctx, hx_dtype dtype, const void* q, const void* k,
+                           const void* v, void* o, float* lse, int bh, int seq_len,
+                           int head_dim, float scale, int causal);
+
+/* Bytes of device workspace hx_*_bwd needs for this problem. */
+int hx_attn_bwd_workspace_size(hx_dtype dtype, const hx_attn_shape* shape, uint64_t* bytes);
+
+/* dq, dk, dv of the forward above for upstream gradient dout, from the saved
+ * o and lse. workspace may be NULL: the call then takes it from the context's
+ * arena and gives it back. Returns the gradients in the order [q, k, v] of
+ * FlashAttentionOp::backward (src/ops/flash_attention.rs:38), with the
+ * softmax scale applied to dq and dk. */
+int hx_flash_attention_bwd(hx_ctx* ctx, hx_dtype dtype, const void* q, const void* k,
+                           const void* v, const void* o, const void* dout, const float* lse,
+                           void* dq, void* dk, void* dv, void* workspace,
+                           uint64_t workspace_bytes, int bh, int seq_len, int head_dim,
+                           float scale, int causal);
+
+/* ---- fused attention on strided [B, H, S, D] views ------------------------- */
+/* lse is contiguous [B, H, S]. */
+int hx_attn_fwd_strided(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape, const void* q,
+                        const void* k, const void* v, void* o, float* lse, float scale,
+                        int causal);
+int hx_attn_bwd_strided(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape, const void* q,
+                        const void* k, const void* v, const void* o, const void* dout,
+                        const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                        uint64_t workspace_bytes, float scale, int causal);
+
+/* ---- rotary embedding (src/kernels/rope.rs) ---------------------------------- */
+/* Rotates interleaved pairs (2i, 2i+1) of every [.., S, D] row by
+ * theta = s * base^(-2i/D), s the row's sequence index; bwd rotates by -theta.
+ * x and out may alias. */
+int hx_rope_fwd(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape, const void* x, void* out,
+                float base);
+int hx_rope_bwd(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape, const void* g, void* out,
+                float base);
+
+/* ---- multi-GPU head sharding ------------------------------------------------------ */
+/* After an all-gather of per-rank head shards, shards holds n_shards
+ * contiguous blocks [B, H_shard, S, D]; writes them as [B, H, S, D]
+ * (out_layout 0) or [B, S, H, D] (out_layout 1, the merged-heads layout of
+ * src/nn/attention.rs:91-94), H = n_shards * H_shard. */
+int hx_reassemble_heads(hx_ctx* ctx, hx_dtype dtype, const void* shards, void* out, int n_shards,
+                        int B, int H_shard, int S, int D, int out_layout);
+
+/* ---- diagnostics --------------------------------------------------------------- */
+/* Number of kernels this context has launched so far. */
+uint64_t hx_kernel_launches(const hx_ctx* ctx);
+/* Which kernel family the last attention call used on this context:
+ * 0 none, 1 SIMT (f32 / any head_dim), 2 tcgen05 (bf16, head_dim 64 or 128). */
+int hx_last_path(const hx_ctx* ctx);
+/* Forces the SIMT kernels (1) or restores automatic selection (0). */
+int hx_set_force_simt(hx_ctx* ctx, int force);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HAELIXE_CUDA_H */

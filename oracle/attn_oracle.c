@@ -1,0 +1,176 @@
+/*
+ * CPU oracle for haelixe's fused attention path: a C restatement of the
+ * reference's own CPU math (the crate is Rust + WGSL and cannot be built
+ * or run in this environment).
+ *
+ * TEST INFRASTRUCTURE ONLY. Only the test-suite, the smoke check and the
+ * CPU-baseline leg of the benchmark load this library; the product library
+ * (haelixe_b200/csrc) never links or calls it.
+ *
+ * What it restates (paths inside the reference project):
+ *   - forward  : src/ops/flash_attention.rs:18-19 (scores = scale Q K^T,
+ *                softmax) + src/gpu/shaders/flash_attention.wgsl:19-123
+ *                (same math as an online softmax), O = P V;
+ *   - backward : src/ops/flash_attention.rs:16-39 with
+ *                src/kernels/activations.rs:154-188 (softmax Jacobian);
+ *   - matmul   : src/kernels/matmul.rs:31-126 (64^3 blocks, i-p-j order);
+ *   - softmax  : src/kernels/activations.rs:102-152 / softmax.rs:20-44;
+ *   - RoPE     : src/kernels/rope.rs:5-82 (interleaved pairs);
+ *   - bf16     : round-to-nearest-even, the rounding of `half::bf16::from_f32`
+ *                (half 2.7.1, used at src/tensor.rs:706).
+ * Deliberate departures (each a defect of the reference, noted in the
+ * functions): true transposes instead of the stride-ignoring CPU matmul,
+ * dQ/dK multiplied by `scale` (switch `ref_compat` off), and a causal mask.
+ *
+ * Parity status: PARTIALLY PINNED. The softmax forward/backward kernels are
+ * pinned to the reference's golden vectors (haelixe-lab/src/main.rs:35-209)
+ * and finite-difference tolerances (tests/tensor_tests.rs:120-190). The
+ * reference has no attention test and no runnable attention path, so the
+ * attention outputs and gradients themselves are pinned only by the
+ * composition of those kernels, by finite differences and by an independent
+ * f64 evaluation of the same formulas.
+ */
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <unistd.h>
+
+#define ORA_BLOCK 64 /* src/kernels/matmul.rs:6-8 */
+
+static int g_threads = 0;
+
+void ora_set_threads(int n) { g_threads = n; }
+
+int ora_num_threads(void) {
+    if (g_threads > 0) return g_threads;
+    long n = sysconf(_SC_NPROCESSORS_ONLN);
+    return n > 0 ? (int)n : 1;
+}
+
+typedef void (*ora_task_fn)(void* ctx, long begin, long end);
+
+typedef struct {
+    ora_task_fn fn;
+    void* ctx;
+    long begin, end;
+} ora_job;
+
+static void* ora_worker(void* arg) {
+    ora_job* j = (ora_job*)arg;
+    if (j->begin < j->end) j->fn(j->ctx, j->begin, j->end);
+    return NULL;
+}
+
+/* Split [0, n) into one contiguous chunk per thread (the rayon pool of the
+ * reference also defaults to one worker per core). */
+static void ora_parallel_for(long n, ora_task_fn fn, void* ctx) {
+    int t = ora_num_threads();
+    if (t > n) t = (int)n;
+    if (t <= 1) {
+        if (n > 0) fn(ctx, 0, n);
+        return;
+    }
+    pthread_t th[512];
+    ora_job jobs[512];
+    if (t > 512) t = 512;
+    const long chunk = (n + t - 1) / t;
+    for (int i = 0; i < t; ++i) {
+        jobs[i].fn = fn;
+        jobs[i].ctx = ctx;
+        jobs[i].begin = i * chunk;
+        jobs[i].end = (i + 1) * chunk < n ? (i + 1) * chunk : n;
+    }
+    for (int i = 1; i < t; ++i) pthread_create(&th[i], NULL, ora_worker, &jobs[i]);
+    ora_worker(&jobs[0]);
+    for (int i = 1; i < t; ++i) pthread_join(th[i], NULL);
+}
+
+/* f32 restatement (the "port"). */
+#define REAL float
+#define SFX
+#define ORA_EXP expf
+#define ORA_LOG logf
+#include "attn_oracle_impl.h"
+#undef REAL
+#undef SFX
+#undef ORA_EXP
+#undef ORA_LOG
+
+/* f64 evaluation of the same formulas (cross-check of the port). */
+#define REAL double
+#define SFX _f64
+#define ORA_EXP exp
+#define ORA_LOG log
+#include "attn_oracle_impl.h"
+#undef REAL
+#undef SFX
+#undef ORA_EXP
+#undef ORA_LOG
+
+/* Row softmax over `rows` rows of length n (out of place), exported for the
+ * golden-vector checks of the reference's softmax kernel. */
+void ora_softmax(const float* x, float* y, long rows, long n) {
+    memcpy(y, x, sizeof(float) * rows * n);
+    softmax_rows_inplace(y, NULL, rows, n);
+}
+
+/* softmax_backward(dy, y) -> dx, src/kernels/activations.rs:154-188. */
+void ora_softmax_backward(const float* dy, const float* y, float* dx, long rows, long n) {
+    memcpy(dx, dy, sizeof(float) * rows * n);
+    softmax_backward_inplace(dx, y, rows, n);
+}
+
+/* RoPE forward, src/kernels/rope.rs:5-44. x is [tokens, D] with the
+ * sequence position m = token % S (rope.rs:24); pairs (2i, 2i+1) rotate by
+ * theta = m * base^(-(2i)/D) computed in f32 with powf/cosf/sinf
+ * (rope.rs:28-31), one multiply and one add/sub per term (rope.rs:37-38). */
+void ora_rope_fwd(const float* x, float* out, long tokens, int S, int D, float base) {
+    for (long t = 0; t < tokens; ++t) {
+        const float m = (float)(t % S);
+        const long off = t * D;
+        for (int i = 0; i < D / 2; ++i) {
+            const float exponent = -((float)(2 * i)) / (float)D;
+            const float theta = m * powf(base, exponent);
+            const float c = cosf(theta), s = sinf(theta);
+            const float x0 = x[off + 2 * i], x1 = x[off + 2 * i + 1];
+            const float a = x0 * c, b = x1 * s, e = x0 * s, f = x1 * c;
+            out[off + 2 * i] = a - b;
+            out[off + 2 * i + 1] = e + f;
+        }
+    }
+}
+
+/* RoPE backward, src/kernels/rope.rs:46-82: the same rotation by -theta
+ * (rope.rs:67). */
+void ora_rope_bwd(const float* g, float* out, long tokens, int S, int D, float base) {
+    for (long t = 0; t < tokens; ++t) {
+        const float m = (float)(t % S);
+        const long off = t * D;
+        for (int i = 0; i < D / 2; ++i) {
+            const float exponent = -((float)(2 * i)) / (float)D;
+            const float theta = -(m * powf(base, exponent));
+            const float c = cosf(theta), s = sinf(theta);
+            const float g0 = g[off + 2 * i], g1 = g[off + 2 * i + 1];
+            const float a = g0 * c, b = g1 * s, e = g0 * s, f = g1 * c;
+            out[off + 2 * i] = a - b;
+            out[off + 2 * i + 1] = e + f;
+        }
+    }
+}
+
+/* f32 -> bf16 -> f32 with round-to-nearest-even; NaN stays NaN. */
+void ora_round_bf16(const float* x, float* y, long n) {
+    for (long i = 0; i < n; ++i) {
+        uint32_t u;
+        memcpy(&u, &x[i], 4);
+        if ((u & 0x7fffffffu) > 0x7f800000u) {
+            u = (u | 0x00400000u) & 0xffff0000u;
+        } else {
+            u += 0x7fffu + ((u >> 16) & 1u);
+            u &= 0xffff0000u;
+        }
+        memcpy(&y[i], &u, 4);
+    }
+}
