@@ -59,6 +59,7 @@ SIGNATURES = {
     "hx_ctx_device": (_I, [_P, ctypes.POINTER(_I)]),
     "hx_ctx_stream": (_P, [_P]),
     "hx_ctx_set_stream": (_I, [_P, _P]),
+    "hx_ctx_use_own_stream": (_I, [_P]),
     "hx_sync": (_I, [_P]),
     "hx_last_error": (_I, [_P, ctypes.c_char_p, ctypes.c_size_t]),
     "hx_bin_size": (_U64, [_U64]),

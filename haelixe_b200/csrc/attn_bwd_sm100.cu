@@ -3,6 +3,8 @@
 
 namespace hx {
 
+bool sm100_bwd_supported(hx_dtype, const AttnDims&) { return false; }
+
 uint64_t sm100_bwd_workspace_bytes(const AttnDims&) { return 0; }
 
 cudaError_t sm100_attn_bwd(cudaStream_t, int, DeviceStatus*, const AttnDims&, const void*,

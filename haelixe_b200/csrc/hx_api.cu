@@ -173,7 +173,7 @@ int hx_ctx_destroy(hx_ctx* c) {
     if (c == nullptr) return HX_OK;
     DeviceGuard g(c->device);
     if (c->own_stream) cudaStreamSynchronize(c->own_stream);
-    if (c->stream && c->stream != c->own_stream) cudaStreamSynchronize(c->stream);
+    if (c->stream != c->own_stream) cudaStreamSynchronize(c->stream);
     if (c->own_stream) {
         std::lock_guard<std::mutex> lk(c->arena.mu);
         for (auto& kv : c->arena.free_list)
@@ -200,7 +200,13 @@ void* hx_ctx_stream(hx_ctx* c) { return c ? (void*)c->stream : nullptr; }
 
 int hx_ctx_set_stream(hx_ctx* c, void* stream) {
     if (c == nullptr) return HX_ERR_INVALID;
-    c->stream = stream ? (cudaStream_t)stream : c->own_stream;
+    c->stream = (cudaStream_t)stream;
+    return HX_OK;
+}
+
+int hx_ctx_use_own_stream(hx_ctx* c) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    c->stream = c->own_stream;
     return HX_OK;
 }
 
@@ -389,7 +395,7 @@ int hx_attn_bwd_workspace_size(hx_dtype dt, const hx_attn_shape* shape, uint64_t
     if (validate_dtype(nullptr, dt, "") || validate_shape(nullptr, shape, "")) return HX_ERR_INVALID;
     const hx::AttnDims d = hx::dims_of(*shape);
     uint64_t n = simt_ws_bytes(d);
-    if (hx::sm100_supported(dt, d)) n = std::max(n, hx::sm100_bwd_workspace_bytes(d));
+    if (hx::sm100_bwd_supported(dt, d)) n = std::max(n, hx::sm100_bwd_workspace_bytes(d));
     *bytes = n;
     return HX_OK;
 }
@@ -408,7 +414,7 @@ int hx_attn_bwd_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, cons
     DeviceGuard g(c->device);
     LaunchCount lc(c);
     const hx::AttnDims d = hx::dims_of(*shape);
-    const bool fast = !c->force_simt && hx::sm100_supported(dt, d) &&
+    const bool fast = !c->force_simt && hx::sm100_bwd_supported(dt, d) &&
                       tma_layout_ok(d, {q, k, v, o, dout, dq, dk, dv});
     const uint64_t need = fast ? hx::sm100_bwd_workspace_bytes(d) : simt_ws_bytes(d);
     void* ws = workspace;

@@ -76,6 +76,7 @@ bool sm100_supported(hx_dtype dt, const AttnDims& d);
 cudaError_t sm100_attn_fwd(cudaStream_t st, int sm_count, DeviceStatus* status,
                            const AttnDims& d, const void* q, const void* k, const void* v,
                            void* o, float* lse, float scale, int causal);
+bool sm100_bwd_supported(hx_dtype dt, const AttnDims& d);
 uint64_t sm100_bwd_workspace_bytes(const AttnDims& d);
 cudaError_t sm100_attn_bwd(cudaStream_t st, int sm_count, DeviceStatus* status,
                            const AttnDims& d, const void* q, const void* k, const void* v,

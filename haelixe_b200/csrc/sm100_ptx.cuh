@@ -92,6 +92,17 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     return mbar_wait_slow(bar, parity, abort_flag, status, site);
 }
 
+// Waits with a time limit only (ignores the abort flag): used on the way out
+// to let this CTA's own asynchronous copies / MMAs finish before its shared
+// memory and tensor memory are released.
+__device__ __noinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer();
+    for (uint32_t n = 1;; ++n) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((n & 31u) == 0 && globaltimer() - t0 > kWaitLimitNs) return false;
+    }
+}
+
 // ---- TMA (tiled tensor loads into this CTA's shared memory, no multicast) ----
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -93,8 +93,10 @@ int hx_ctx_destroy(hx_ctx* ctx);
 int hx_ctx_device(const hx_ctx* ctx, int* device);
 /* The cudaStream_t the context enqueues on (as void*). */
 void* hx_ctx_stream(hx_ctx* ctx);
-/* Replace the stream (NULL restores the context's own stream). */
+/* Enqueue on `stream` (a cudaStream_t; NULL is CUDA's legacy default stream). */
 int hx_ctx_set_stream(hx_ctx* ctx, void* stream);
+/* Go back to the context's own stream. */
+int hx_ctx_use_own_stream(hx_ctx* ctx);
 /* Blocks until the stream drains; reports a pending device timeout. */
 int hx_sync(hx_ctx* ctx);
 /* Copies the last error text (NUL-terminated) into buf. */
