@@ -4,15 +4,16 @@
 // (src/gpu/shaders/flash_attention.wgsl:19-123, 16x16 tiles, D fixed at 64)
 // behind GpuContext::flash_attention_gpu (src/gpu/mod.rs:1336-1418).
 //
-// One CTA = 320 threads and two 128-row query tiles of one (batch, head):
+// One CTA = 384 threads and two 128-row query tiles of one (batch, head):
 //   warp 0      TMA producer: Q tiles once, then a K/V ring of STAGES tiles
 //               (128 keys each) with 128-byte swizzle; full/empty mbarriers.
 //   warp 1      MMA issuer (one thread): S_w = Q_w K_j^T (SS UMMA, M=N=128)
 //               into TMEM, then O_w += P_w V_j (TS UMMA: P read from TMEM,
 //               V from smem as an MN-major operand). tcgen05.commit signals
 //               the consumers and frees K/V slots.
-//               Warp 0 also allocates TMEM (512 columns: S0 | S1 | O0 | O1).
-//   warps 2-5   softmax warpgroup for query tile 0, warps 6-9 for tile 1:
+//               Warp 0 also allocates TMEM (512 columns: S0 | S1 | O0 | O1);
+//               warps 2-3 only hold registers for the split below.
+//   warps 4-7   softmax warpgroup for query tile 0, warps 8-11 for tile 1:
 //               lane l of warp w owns query row 32*(w%4)+l of its tile (the
 //               TMEM lane quadrant warp w may access), so row
 //               max and row sum need no shuffles. P is written back over S
@@ -39,7 +40,16 @@ using namespace ptx;
 constexpr int BM = 128;  // query rows per softmax warpgroup (UMMA M)
 constexpr int BN = 128;  // keys per K/V tile
 constexpr int NWG = 2;   // query tiles (softmax warpgroups) per CTA
-constexpr int kThreads = 320;  // 2 control warps + 2 softmax warpgroups
+constexpr int kThreads = 384;  // control warpgroup + 2 softmax warpgroups
+// Register split (setmaxnreg): the launch gives every thread kRegsLaunch;
+// the control warpgroup (TMA, MMA, TMEM allocation) drops to kRegsCtl and
+// the softmax warpgroups rise to kRegsSoftmax. Per SM sub-partition (one
+// control warp + two softmax warps) that is 56 + 2*224 = 504 <= 3*168.
+constexpr int kRegsLaunch = 168;
+constexpr int kRegsCtl = 56;
+constexpr int kRegsSoftmax = 224;
+static_assert(128 * kRegsCtl + 256 * kRegsSoftmax <= kThreads * kRegsLaunch,
+              "register split exceeds the launch allocation");
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the max grows by > 2^8
@@ -81,7 +91,7 @@ struct FwdParams {
 __device__ __forceinline__ uint32_t bar_addr(const uint64_t& b) { return smem_addr(&b); }
 
 template <int D>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, const FwdParams p) {
     using C = Cfg<D>;
@@ -136,6 +146,12 @@ __global__ void __maxnreg__(200)
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
 
+    if (warp < 4) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegsCtl));
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsSoftmax));
+    }
+
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
@@ -173,9 +189,16 @@ __global__ void __maxnreg__(200)
             for (int j = max(0, nv - C::STAGES); j < nv; ++j)
                 mbar_wait_drain(bar_addr(bars->v_full[j % C::STAGES]), (j / C::STAGES) & 1);
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        __syncwarp();
+        // Teardown inside each role branch: no code is shared across the
+        // register split. Warp 0 releases TMEM once every role is done.
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    } else if (warp < 4) {
+        // ------------------------------------------------------------ MMA issuer (warp 1, lane 0)
+        if (warp == 1 && lane == 0) {
             constexpr uint32_t idS = idesc_bf16_f32(BM, BN, false, false);
             constexpr uint32_t idO = idesc_bf16_f32(BM, D, false, true);
             const uint32_t sQ = smem_addr(sm + C::Q_OFF), sK = smem_addr(sm + C::K_OFF),
@@ -242,9 +265,12 @@ __global__ void __maxnreg__(200)
             umma_commit(bar_addr(bars->done));
             mbar_wait_drain(bar_addr(bars->done), 0);
         }
+        __syncwarp();
+        tc_fence_before();
+        __syncthreads();
     } else {
         // ------------------------------------------------------------ softmax
-        const int w = (warp - 2) / 4;
+        const int w = (warp - 4) / 4;
         const int wi = warp % 4;
         const int r = wi * 32 + lane;
         const int row = m0 + w * BM + r;
@@ -357,13 +383,8 @@ __global__ void __maxnreg__(200)
             if (store)
                 p.lse[((int64_t)b * p.H + h) * p.S + row] = (m_run + __log2f(l_run)) * kLn2;
         }
-    }
-
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-        tc_fence_after();
-        tmem_dealloc(tmem, 512);
+        tc_fence_before();
+        __syncthreads();
     }
 }
 

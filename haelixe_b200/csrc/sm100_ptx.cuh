@@ -68,7 +68,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // CTA's abort flag is raised or after kWaitLimitNs; the first waiter to time
 // out raises the flag and records `site` in the device status word, so every
 // role of the CTA unwinds and the host reports HX_ERR_TIMEOUT.
-__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+__device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                             DeviceStatus* status, int site) {
     const uint64_t t0 = globaltimer();
     for (uint32_t n = 1;; ++n) {
@@ -95,7 +95,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 // Waits with a time limit only (ignores the abort flag): used on the way out
 // to let this CTA's own asynchronous copies / MMAs finish before its shared
 // memory and tensor memory are released.
-__device__ __noinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
     const uint64_t t0 = globaltimer();
     for (uint32_t n = 1;; ++n) {
         if (mbar_try_wait(bar, parity)) return true;
