@@ -1,16 +1,587 @@
-// tcgen05 attention backward (bf16, head_dim 64/128). Placeholder.
-#include "hx_internal.h"
+// tcgen05 fused attention backward for sm_100a (bf16 I/O, f32 accumulation,
+// head_dim 64 or 128, optional causal mask). Replaces the reference's
+// composite backward (src/ops/flash_attention.rs:16-39: recompute P, five
+// batched matmuls and a softmax-Jacobian kernel over materialised S x S
+// matrices) with three launches that never materialise S x S:
+//
+//   pre   delta[q] = sum_d dO[q,d] O[q,d]  (the `dot` of the softmax backward,
+//         src/kernels/activations.rs:170-176) and zero the f32 dQ accumulator;
+//   main  one CTA per (128-key tile, head, batch), K and V resident in smem,
+//         looping over query tiles of BQ rows:
+//           S^T  = K Q^T      (SS UMMA, M=128 keys, N=BQ)      -> TMEM
+//           dP^T = V dO^T     (SS UMMA)                         -> TMEM
+//           P^T  = exp2(S^T * scale*log2e - lse*log2e) (mask)   -> TMEM (bf16)
+//           dV  += P^T dO     (TS UMMA, A from TMEM, B = dO MN-major)
+//           dS^T = P^T (dP^T - delta)                           -> TMEM + smem (bf16)
+//           dK  += dS^T Q     (TS UMMA)
+//           dQ   = dS K       (SS UMMA from the smem copy of dS; for D=128 as
+//                              dQ^T = K^T dS^T so M = D = 128)  -> TMEM (2 buffers)
+//         a second warpgroup drains each dQ tile from TMEM into the f32
+//         accumulator with atomics while the tensor core moves on;
+//   post  dQ = bf16(scale * accumulator), dK already carries the scale.
+// The scale on dQ and dK is the factor the reference's backward omits
+// (flash_attention.rs:31,34-36).
+//
+// Warp roles of `main` (384 threads): warp 0 TMA producer (its lanes also
+// stage lse/delta of each query tile in smem), warp 1 MMA issuer (one
+// thread), warp 2 TMEM allocator, warps 4-7 the P/dS warpgroup (thread =
+// key row = TMEM lane), warps 8-11 the dQ drain warpgroup. All mbarrier
+// waits are bounded (sm100_ptx.cuh).
+#include <math.h>
+
+#include "sm100_ptx.cuh"
+#include "tma_host.h"
 
 namespace hx {
+namespace {
 
-bool sm100_bwd_supported(hx_dtype, const AttnDims&) { return false; }
+using namespace ptx;
 
-uint64_t sm100_bwd_workspace_bytes(const AttnDims&) { return 0; }
+constexpr int BK = 128;  // keys per CTA (UMMA M of S^T, dP^T, dV, dK)
+constexpr int kThreads = 384;
+constexpr float kLog2e = 1.4426950408889634f;
 
-cudaError_t sm100_attn_bwd(cudaStream_t, int, DeviceStatus*, const AttnDims&, const void*,
-                           const void*, const void*, const void*, const void*, const float*,
-                           void*, void*, void*, void*, float, int) {
-    return cudaErrorNotSupported;
+template <int D>
+struct BCfg {
+    static constexpr int BQ = D == 128 ? 64 : 128;  // queries per inner tile
+    static constexpr bool DQ_T = D == 128;           // dQ computed transposed (M = D)
+    static constexpr int QST = 2;                    // Q/dO ring depth
+    static constexpr int CHUNK_K = BK * 128;         // bytes of a 64-column chunk of a K/V tile
+    static constexpr int CHUNK_Q = BQ * 128;         // ... of a Q/dO tile
+    static constexpr int CHUNK_DS = BK * 128;        // ... of the dS^T tile (64 queries wide)
+    static constexpr int KT = BK * D * 2;
+    static constexpr int QT = BQ * D * 2;
+    static constexpr int DST = BK * BQ * 2;
+    static constexpr int K_OFF = 0;
+    static constexpr int V_OFF = K_OFF + KT;
+    static constexpr int Q_OFF = V_OFF + KT;
+    static constexpr int DO_OFF = Q_OFF + QST * QT;
+    static constexpr int DS_OFF = DO_OFF + QST * QT;
+    static constexpr int LSE_OFF = DS_OFF + DST;
+    static constexpr int DEL_OFF = LSE_OFF + QST * BQ * 4;
+    static constexpr int BAR_OFF = DEL_OFF + QST * BQ * 4;
+    static constexpr int SMEM = BAR_OFF + 256 + 1024;
+    // TMEM columns
+    static constexpr int DQ_COLS = DQ_T ? BQ : D;
+    static constexpr uint32_t C_S = 0, C_DP = BQ, C_DQ0 = 2 * BQ, C_DQ1 = 2 * BQ + DQ_COLS,
+                              C_DV = 2 * BQ + 2 * DQ_COLS, C_DK = C_DV + D;
+    static_assert(C_DK + D <= 512, "TMEM budget");
+};
+
+struct BBars {
+    uint64_t kv_full;
+    uint64_t q_full[2], q_empty[2];
+    uint64_t s_full, dp_full, p_full, ds_full;
+    uint64_t dq_full[2], dq_empty[2];
+    uint64_t acc_done, done;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+struct BwdParams {
+    const float* lse;    // [B,H,S]
+    const float* delta;  // [B,H,S]
+    float* dq_acc;       // [B,H,S,D] f32
+    __nv_bfloat16* dk;
+    __nv_bfloat16* dv;
+    int64_t sb, sh, ss;  // strides of dk/dv (elements)
+    int S, H;
+    float scale;
+    int causal;
+    DeviceStatus* status;
+};
+
+__device__ __forceinline__ uint32_t bar_addr(const uint64_t& b) { return smem_addr(&b); }
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* r) {
+#pragma unroll
+    for (int c = 0; c < N; c += 32) tmem_ld32(taddr + c, r + c);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                    const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                    const BwdParams p) {
+    using C = BCfg<D>;
+    constexpr int BQ = C::BQ;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    BBars* bars = (BBars*)(sm + C::BAR_OFF);
+    float* s_lse = (float*)(sm + C::LSE_OFF);
+    float* s_del = (float*)(sm + C::DEL_OFF);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int k0 = blockIdx.x * BK;
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int64_t bh = (int64_t)b * p.H + h;
+    const int i_start = p.causal ? k0 / BQ : 0;
+    const int n_it = (p.S + BQ - 1) / BQ - i_start;
+    volatile int* abort_flag = &bars->abort_flag;
+
+    if (threadIdx.x == 0) {
+        bars->abort_flag = 0;
+        mbar_init(bar_addr(bars->kv_full), 1);
+        for (int s = 0; s < C::QST; ++s) {
+            mbar_init(bar_addr(bars->q_full[s]), 1 + 32);
+            mbar_init(bar_addr(bars->q_empty[s]), 1);
+        }
+        mbar_init(bar_addr(bars->s_full), 1);
+        mbar_init(bar_addr(bars->dp_full), 1);
+        mbar_init(bar_addr(bars->p_full), 128);
+        mbar_init(bar_addr(bars->ds_full), 128);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(bar_addr(bars->dq_full[s]), 1);
+            mbar_init(bar_addr(bars->dq_empty[s]), 128);
+        }
+        mbar_init(bar_addr(bars->acc_done), 1);
+        mbar_init(bar_addr(bars->done), 1);
+        fence_mbar_init();
+        fence_proxy_async();
+    }
+    if (warp == 2) {
+        tmem_alloc(smem_addr(&bars->tmem_base), 512);
+        tmem_relinquish();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tq);
+        prefetch_tmap(&tk);
+        prefetch_tmap(&tv);
+        prefetch_tmap(&tdo);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        const uint32_t kvb = bar_addr(bars->kv_full);
+        if (lane == 0) {
+            mbar_arrive_expect_tx(kvb, 2 * C::KT);
+            for (int c = 0; c < D / 64; ++c) {
+                tma_load_4d(smem_addr(sm + C::K_OFF + c * C::CHUNK_K), &tk, kvb, c * 64, k0, h, b);
+                tma_load_4d(smem_addr(sm + C::V_OFF + c * C::CHUNK_K), &tv, kvb, c * 64, k0, h, b);
+            }
+        }
+        int issued = 0;
+        for (int it = 0; it < n_it; ++it) {
+            const int st = it % C::QST;
+            const uint32_t ph = (it / C::QST) & 1;
+            const int q0 = (i_start + it) * BQ;
+            if (!mbar_wait(bar_addr(bars->q_empty[st]), ph ^ 1, abort_flag, p.status, 40)) break;
+            const uint32_t qb = bar_addr(bars->q_full[st]);
+            if (lane == 0) {
+                mbar_arrive_expect_tx(qb, 2 * C::QT);
+                for (int c = 0; c < D / 64; ++c) {
+                    tma_load_4d(smem_addr(sm + C::Q_OFF + st * C::QT + c * C::CHUNK_Q), &tq, qb,
+                                c * 64, q0, h, b);
+                    tma_load_4d(smem_addr(sm + C::DO_OFF + st * C::QT + c * C::CHUNK_Q), &tdo, qb,
+                                c * 64, q0, h, b);
+                }
+            }
+            for (int i = lane; i < BQ; i += 32) {
+                const int q = q0 + i;
+                s_lse[st * BQ + i] = q < p.S ? p.lse[bh * p.S + q] * kLog2e : 0.f;
+                s_del[st * BQ + i] = q < p.S ? p.delta[bh * p.S + q] : 0.f;
+            }
+            mbar_arrive(qb);
+            issued = it + 1;
+        }
+        if (lane == 0) {
+            mbar_wait_drain(kvb, 0);
+            for (int it = max(0, issued - C::QST); it < issued; ++it)
+                mbar_wait_drain(bar_addr(bars->q_full[it % C::QST]), (it / C::QST) & 1);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idSP = idesc_bf16_f32(BK, BQ, false, false);
+            constexpr uint32_t idAcc = idesc_bf16_f32(BK, D, false, true);
+            constexpr uint32_t idDQ =
+                C::DQ_T ? idesc_bf16_f32(D, BQ, true, true) : idesc_bf16_f32(BQ, D, true, true);
+            const uint32_t sK = smem_addr(sm + C::K_OFF), sV = smem_addr(sm + C::V_OFF),
+                           sQ = smem_addr(sm + C::Q_OFF), sDO = smem_addr(sm + C::DO_OFF),
+                           sDS = smem_addr(sm + C::DS_OFF);
+            // S^T or dP^T: A = K or V tile (K-major over D), B = Q or dO tile (K-major).
+            auto issue_sp = [&](uint32_t col, uint32_t a, uint32_t bq) {
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma_ss(tmem + col,
+                            sdesc_sw128(a + (kk / 4) * C::CHUNK_K + (kk % 4) * 32, 16, 1024),
+                            sdesc_sw128(bq + (kk / 4) * C::CHUNK_Q + (kk % 4) * 32, 16, 1024), idSP,
+                            kk > 0);
+            };
+            // dV or dK += (P^T or dS^T from TMEM) x (dO or Q tile, MN-major over D).
+            auto issue_acc = [&](uint32_t col, uint32_t a_col, uint32_t bq, bool first) {
+#pragma unroll
+                for (int kk = 0; kk < BQ / 16; ++kk)
+                    umma_ts(tmem + col, tmem + a_col + kk * 8,
+                            sdesc_sw128(bq + kk * 2048, C::CHUNK_Q, 1024), idAcc,
+                            (first && kk == 0) ? 0u : 1u);
+            };
+            auto issue_dq = [&](uint32_t col) {
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    if (C::DQ_T)  // dQ^T = K^T dS^T: A = K^T (MN-major), B = dS^T (MN-major)
+                        umma_ss(tmem + col, sdesc_sw128(sK + kk * 2048, C::CHUNK_K, 1024),
+                                sdesc_sw128(sDS + kk * 2048, C::CHUNK_DS, 1024), idDQ, kk > 0);
+                    else  // dQ = dS K: A = dS (MN-major), B = K (MN-major)
+                        umma_ss(tmem + col, sdesc_sw128(sDS + kk * 2048, C::CHUNK_DS, 1024),
+                                sdesc_sw128(sK + kk * 2048, C::CHUNK_K, 1024), idDQ, kk > 0);
+                }
+            };
+            bool ok = mbar_wait(bar_addr(bars->kv_full), 0, abort_flag, p.status, 50) &&
+                      mbar_wait(bar_addr(bars->q_full[0]), 0, abort_flag, p.status, 51);
+            if (ok) {
+                tc_fence_after();
+                issue_sp(C::C_S, sK, sQ);
+                umma_commit(bar_addr(bars->s_full));
+                issue_sp(C::C_DP, sV, sDO);
+                umma_commit(bar_addr(bars->dp_full));
+            }
+            for (int it = 0; ok && it < n_it; ++it) {
+                const int st = it % C::QST;
+                const int stn = (it + 1) % C::QST;
+                const uint32_t phn = ((it + 1) / C::QST) & 1;
+                if (!(ok = mbar_wait(bar_addr(bars->p_full), it & 1, abort_flag, p.status, 52))) break;
+                tc_fence_after();
+                issue_acc(C::C_DV, C::C_S, sDO + st * C::QT, it == 0);
+                if (it + 1 < n_it) {
+                    if (!(ok = mbar_wait(bar_addr(bars->q_full[stn]), phn, abort_flag, p.status, 53)))
+                        break;
+                    tc_fence_after();
+                    issue_sp(C::C_S, sK, sQ + stn * C::QT);
+                    umma_commit(bar_addr(bars->s_full));
+                }
+                if (!(ok = mbar_wait(bar_addr(bars->ds_full), it & 1, abort_flag, p.status, 54))) break;
+                tc_fence_after();
+                issue_acc(C::C_DK, C::C_DP, sQ + st * C::QT, it == 0);
+                const int buf = it & 1;
+                if (!(ok = mbar_wait(bar_addr(bars->dq_empty[buf]), ((it >> 1) & 1) ^ 1, abort_flag,
+                                     p.status, 55)))
+                    break;
+                tc_fence_after();
+                issue_dq(buf ? C::C_DQ1 : C::C_DQ0);
+                umma_commit(bar_addr(bars->dq_full[buf]));
+                umma_commit(bar_addr(bars->q_empty[st]));
+                if (it + 1 < n_it) {
+                    issue_sp(C::C_DP, sV, sDO + stn * C::QT);
+                    umma_commit(bar_addr(bars->dp_full));
+                }
+            }
+            umma_commit(bar_addr(bars->acc_done));
+            umma_commit(bar_addr(bars->done));
+            mbar_wait_drain(bar_addr(bars->done), 0);
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ------------------------------------------------------------ P / dS warpgroup
+        const int wi = warp % 4;
+        const int r = wi * 32 + lane;  // key row within the tile (TMEM lane)
+        const int kr = k0 + r;
+        const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
+        const float sl2 = p.scale * kLog2e;
+        uint8_t* ds_row = sm + C::DS_OFF + r * 128;
+        bool ok = true;
+        for (int it = 0; it < n_it; ++it) {
+            const int st = it % C::QST;
+            const uint32_t ph = (it / C::QST) & 1;
+            const int q0 = (i_start + it) * BQ;
+            if (!(ok = mbar_wait(bar_addr(bars->q_full[st]), ph, abort_flag, p.status, 60))) break;
+            if (!(ok = mbar_wait(bar_addr(bars->s_full), it & 1, abort_flag, p.status, 61))) break;
+            tc_fence_after();
+            const float* lse2 = s_lse + st * BQ;
+            const float* del = s_del + st * BQ;
+            const bool need_mask = (q0 + BQ > p.S) || (k0 + BK > p.S) || (p.causal && k0 + BK - 1 > q0);
+            // P^T = exp2(S^T * scale*log2e - lse*log2e), 32 columns at a time. The
+            // packed P of chunk c lands on S columns [c/2, c/2+16), all already read.
+            // P stays in registers for dS: f32 when BQ = 64, packed bf16 when BQ = 128.
+            constexpr bool kKeepF32 = BQ == 64;
+            float pr[kKeepF32 ? BQ : 1];
+            uint32_t pkeep[kKeepF32 ? 1 : BQ / 2];
+#pragma unroll
+            for (int c = 0; c < BQ; c += 32) {
+                uint32_t x[32];
+                tmem_ld32(tl + C::C_S + c, x);
+                tmem_ld_wait();
+                reg_fence<32>(x);
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float p0 = ex2(fmaf(__uint_as_float(x[2 * i]), sl2, -lse2[c + 2 * i]));
+                    float p1 = ex2(fmaf(__uint_as_float(x[2 * i + 1]), sl2, -lse2[c + 2 * i + 1]));
+                    if (need_mask) {
+                        const int qa = q0 + c + 2 * i, qb = qa + 1;
+                        p0 = (qa < p.S && kr < p.S && (!p.causal || kr <= qa)) ? p0 : 0.f;
+                        p1 = (qb < p.S && kr < p.S && (!p.causal || kr <= qb)) ? p1 : 0.f;
+                    }
+                    pk[i] = pack_bf16(p0, p1);
+                    if constexpr (kKeepF32) {
+                        pr[c + 2 * i] = p0;
+                        pr[c + 2 * i + 1] = p1;
+                    } else {
+                        pkeep[c / 2 + i] = pk[i];
+                    }
+                }
+                tmem_st16(tl + C::C_S + c / 2, pk);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(bar_addr(bars->p_full));
+
+            if (!(ok = mbar_wait(bar_addr(bars->dp_full), it & 1, abort_flag, p.status, 62))) break;
+            tc_fence_after();
+            // dS^T = P^T (dP^T - delta) -> TMEM (over dP, same chunk argument) and the
+            // 128-byte-swizzled smem tile read by the dQ MMA.
+#pragma unroll
+            for (int c = 0; c < BQ; c += 32) {
+                uint32_t x[32];
+                tmem_ld32(tl + C::C_DP + c, x);
+                tmem_ld_wait();
+                reg_fence<32>(x);
+                uint32_t dk[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float p0, p1;
+                    if constexpr (kKeepF32) {
+                        p0 = pr[c + 2 * i];
+                        p1 = pr[c + 2 * i + 1];
+                    } else {
+                        p0 = __uint_as_float(pkeep[c / 2 + i] << 16);
+                        p1 = __uint_as_float(pkeep[c / 2 + i] & 0xffff0000u);
+                    }
+                    const float d0 = p0 * (__uint_as_float(x[2 * i]) - del[c + 2 * i]);
+                    const float d1 = p1 * (__uint_as_float(x[2 * i + 1]) - del[c + 2 * i + 1]);
+                    dk[i] = pack_bf16(d0, d1);
+                }
+                tmem_st16(tl + C::C_DP + c / 2, dk);
+                uint8_t* chunk_row = ds_row + (c / 64) * C::CHUNK_DS;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int u = (c % 64) / 8 + j;
+                    *reinterpret_cast<uint4*>(chunk_row + ((u ^ (r & 7)) * 16)) =
+                        make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
+                }
+            }
+            tmem_st_wait();
+            fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
+            tc_fence_before();
+            mbar_arrive(bar_addr(bars->ds_full));
+        }
+        // dK, dV epilogue
+        if (ok && mbar_wait(bar_addr(bars->acc_done), 0, abort_flag, p.status, 63)) {
+            tc_fence_after();
+            const bool store = kr < p.S;
+            const int64_t off = (int64_t)b * p.sb + (int64_t)h * p.sh + (int64_t)kr * p.ss;
+#pragma unroll
+            for (int which = 0; which < 2; ++which) {
+                const uint32_t col = which ? C::C_DK : C::C_DV;
+                const float mul = which ? p.scale : 1.f;
+                __nv_bfloat16* dst = (which ? p.dk : p.dv) + off;
+#pragma unroll
+                for (int c = 0; c < D; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld32(tl + col + c, v);
+                    tmem_ld_wait();
+                    reg_fence<32>(v);
+                    if (store) {
+                        uint4* d4 = reinterpret_cast<uint4*>(dst + c);
+#pragma unroll
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            uint4 o;
+                            o.x = pack_bf16(__uint_as_float(v[8 * q4 + 0]) * mul, __uint_as_float(v[8 * q4 + 1]) * mul);
+                            o.y = pack_bf16(__uint_as_float(v[8 * q4 + 2]) * mul, __uint_as_float(v[8 * q4 + 3]) * mul);
+                            o.z = pack_bf16(__uint_as_float(v[8 * q4 + 4]) * mul, __uint_as_float(v[8 * q4 + 5]) * mul);
+                            o.w = pack_bf16(__uint_as_float(v[8 * q4 + 6]) * mul, __uint_as_float(v[8 * q4 + 7]) * mul);
+                            d4[q4] = o;
+                        }
+                    }
+                }
+            }
+        }
+    } else if (warp >= 8) {
+        // ------------------------------------------------------------ dQ drain warpgroup
+        const int wi = warp % 4;
+        const int r = wi * 32 + lane;  // TMEM lane: d (dQ^T) or query row (dQ)
+        const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
+        for (int it = 0; it < n_it; ++it) {
+            const int buf = it & 1;
+            const int q0 = (i_start + it) * BQ;
+            if (!mbar_wait(bar_addr(bars->dq_full[buf]), (it >> 1) & 1, abort_flag, p.status, 70)) break;
+            tc_fence_after();
+            uint32_t v[C::DQ_COLS];
+            tmem_ld_cols<C::DQ_COLS>(tl + (buf ? C::C_DQ1 : C::C_DQ0), v);
+            tmem_ld_wait();
+            reg_fence<C::DQ_COLS>(v);
+            tc_fence_before();
+            mbar_arrive(bar_addr(bars->dq_empty[buf]));
+            if (C::DQ_T) {
+                // lane r = d; column c = query q0 + c: a warp adds 32 consecutive floats.
+                float* base = p.dq_acc + (bh * p.S + q0) * D + r;
+#pragma unroll
+                for (int c = 0; c < BQ; ++c)
+                    if (q0 + c < p.S) atomicAdd(base + (int64_t)c * D, __uint_as_float(v[c]));
+            } else {
+                const int q = q0 + r;
+                if (q < p.S) {
+                    float4* row = reinterpret_cast<float4*>(p.dq_acc + (bh * p.S + q) * D);
+#pragma unroll
+                    for (int c = 0; c < D; c += 4)
+                        atomicAdd(row + c / 4, make_float4(__uint_as_float(v[c]), __uint_as_float(v[c + 1]),
+                                                           __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3])));
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// delta = rowsum(dO * O) in f32; also zeroes the row of the dQ accumulator.
+template <int D>
+__global__ void __launch_bounds__(256) bwd_pre_kernel(const __nv_bfloat16* __restrict__ o,
+                                                      const __nv_bfloat16* __restrict__ dout,
+                                                      float* __restrict__ delta,
+                                                      float* __restrict__ dq_acc, AttnDims d) {
+    const int64_t rows = (int64_t)d.B * d.H * d.S;
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+    const int lane = threadIdx.x % 32;
+    if (r >= rows) return;
+    const int s = (int)(r % d.S);
+    const int64_t bhi = r / d.S;
+    const int hi = (int)(bhi % d.H), bi = (int)(bhi / d.H);
+    const int64_t off = (int64_t)bi * d.sb + (int64_t)hi * d.sh + (int64_t)s * d.ss;
+    constexpr int PER = D / 32;  // elements per lane (2 or 4)
+    float acc = 0.f;
+    if (PER == 4) {
+        const uint2 a = *reinterpret_cast<const uint2*>(o + off + lane * 4);
+        const uint2 g = *reinterpret_cast<const uint2*>(dout + off + lane * 4);
+        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const float2 x = __bfloat1622float2(a2[i]), y = __bfloat1622float2(g2[i]);
+            acc += x.x * y.x + x.y * y.y;
+        }
+    } else {
+        const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(o + off + lane * 2);
+        const __nv_bfloat162 g = *reinterpret_cast<const __nv_bfloat162*>(dout + off + lane * 2);
+        const float2 x = __bfloat1622float2(a), y = __bfloat1622float2(g);
+        acc = x.x * y.x + x.y * y.y;
+    }
+#pragma unroll
+    for (int w = 16; w > 0; w >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, w);
+    if (lane == 0) delta[r] = acc;
+    float4* z = reinterpret_cast<float4*>(dq_acc + r * D);
+    for (int i = lane; i < D / 4; i += 32) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// dQ = bf16(scale * accumulator); 8 elements per thread.
+template <int D>
+__global__ void __launch_bounds__(256) bwd_post_kernel(const float* __restrict__ dq_acc,
+                                                       __nv_bfloat16* __restrict__ dq, AttnDims d,
+                                                       float scale) {
+    const int64_t n8 = (int64_t)d.B * d.H * d.S * (D / 8);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int c8 = (int)(i % (D / 8));
+        const int64_t r = i / (D / 8);
+        const int s = (int)(r % d.S);
+        const int64_t bhi = r / d.S;
+        const int hi = (int)(bhi % d.H), bi = (int)(bhi / d.H);
+        const float4* src = reinterpret_cast<const float4*>(dq_acc + r * D + c8 * 8);
+        const float4 a = src[0], c = src[1];
+        uint4 o;
+        o.x = ptx::pack_bf16(a.x * scale, a.y * scale);
+        o.y = ptx::pack_bf16(a.z * scale, a.w * scale);
+        o.z = ptx::pack_bf16(c.x * scale, c.y * scale);
+        o.w = ptx::pack_bf16(c.z * scale, c.w * scale);
+        *reinterpret_cast<uint4*>(dq + (int64_t)bi * d.sb + (int64_t)hi * d.sh + (int64_t)s * d.ss +
+                                  c8 * 8) = o;
+    }
+}
+
+uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
+
+template <int D>
+cudaError_t launch(cudaStream_t st, int sm_count, DeviceStatus* status, const AttnDims& d,
+                   const void* q, const void* k, const void* v, const void* o, const void* dout,
+                   const float* lse, void* dq, void* dk, void* dv, void* ws, float scale,
+                   int causal) {
+    using C = BCfg<D>;
+    const int64_t rows = (int64_t)d.B * d.H * d.S;
+    float* delta = (float*)ws;
+    float* dq_acc = (float*)((uint8_t*)ws + align256((uint64_t)rows * 4));
+    bwd_pre_kernel<D><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(
+        (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, delta, dq_acc, d);
+    note_launch();
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+
+    CUtensorMap tq, tk, tv, tdo;
+    if (!make_tmap_bhsd(&tq, q, d.B, d.H, d.S, D, d.sb, d.sh, d.ss, 64, C::BQ) ||
+        !make_tmap_bhsd(&tdo, dout, d.B, d.H, d.S, D, d.sb, d.sh, d.ss, 64, C::BQ) ||
+        !make_tmap_bhsd(&tk, k, d.B, d.H, d.S, D, d.sb, d.sh, d.ss, 64, BK) ||
+        !make_tmap_bhsd(&tv, v, d.B, d.H, d.S, D, d.sb, d.sh, d.ss, 64, BK))
+        return cudaErrorInvalidValue;
+    e = cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM);
+    if (e != cudaSuccess) return e;
+    BwdParams prm;
+    prm.lse = lse;
+    prm.delta = delta;
+    prm.dq_acc = dq_acc;
+    prm.dk = (__nv_bfloat16*)dk;
+    prm.dv = (__nv_bfloat16*)dv;
+    prm.sb = d.sb;
+    prm.sh = d.sh;
+    prm.ss = d.ss;
+    prm.S = d.S;
+    prm.H = d.H;
+    prm.scale = scale;
+    prm.causal = causal;
+    prm.status = status;
+    dim3 grid((d.S + BK - 1) / BK, d.H, d.B);
+    attn_bwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, tdo, prm);
+    note_launch();
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+
+    const int64_t n8 = rows * (D / 8);
+    int64_t blocks = (n8 + 255) / 256;
+    if (blocks > (int64_t)sm_count * 32) blocks = (int64_t)sm_count * 32;
+    bwd_post_kernel<D><<<(unsigned)blocks, 256, 0, st>>>(dq_acc, (__nv_bfloat16*)dq, d, scale);
+    note_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool sm100_bwd_supported(hx_dtype dt, const AttnDims& d) {
+    return dt == HX_BF16 && (d.D == 64 || d.D == 128);
+}
+
+uint64_t sm100_bwd_workspace_bytes(const AttnDims& d) {
+    const uint64_t rows = (uint64_t)d.B * d.H * d.S;
+    return align256(rows * 4) + align256(rows * (uint64_t)d.D * 4);
+}
+
+cudaError_t sm100_attn_bwd(cudaStream_t st, int sm_count, DeviceStatus* status,
+                           const AttnDims& d, const void* q, const void* k, const void* v,
+                           const void* o, const void* dout, const float* lse, void* dq, void* dk,
+                           void* dv, void* workspace, float scale, int causal) {
+    if (d.D == 64)
+        return launch<64>(st, sm_count, status, d, q, k, v, o, dout, lse, dq, dk, dv, workspace,
+                          scale, causal);
+    if (d.D == 128)
+        return launch<128>(st, sm_count, status, d, q, k, v, o, dout, lse, dq, dk, dv, workspace,
+                           scale, causal);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace hx

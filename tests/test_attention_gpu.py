@@ -64,8 +64,12 @@ def test_fwd_bwd_matches_oracle(BH, S, D, causal, dtype):
     q, k, v, do = (_host((BH, S, D), seed + i, dtype) for i in range(4))
     scale = 1.0 / math.sqrt(D)
     qd, kd, vd, dod = (_dev(a, dtype) for a in (q, k, v, do))
+    ctx = hx.context()
+    expect = "tcgen05" if (dtype == torch.bfloat16 and D in (64, 128)) else "simt"
     o, lse = hx.attn_forward(qd, kd, vd, scale, causal)
+    assert ctx.last_path == expect
     dq, dk, dv = hx.attn_backward(qd, kd, vd, o, lse, dod, scale, causal)
+    assert ctx.last_path == expect
     torch.cuda.synchronize()
     ro, rlse = ora.attn_fwd(q, k, v, scale, causal)
     rdq, rdk, rdv = ora.attn_bwd(q, k, v, do, scale, causal)
@@ -203,10 +207,11 @@ def _sampled_full_size(B, H, S, D, causal, rope_base=None, samples=((0, 0),)):
     dq, dk, dv = hx.attn_backward(q, k, v, o, lse, do, scale, causal)
     torch.cuda.synchronize()
     # identities over every head: sum_j dK_j = 0, sum_j dV_j = sum_i dO_i
-    dks = dk.float().sum(2)
-    assert dks.abs().max().item() < 0.5, dks.abs().max().item()
+    dks, dk_l1 = dk.float().sum(2), dk.float().abs().sum(2)
+    assert (dks.abs() <= 0.02 * dk_l1 + 1e-3).all(), (dks.abs() / dk_l1).max().item()
     dvs, dos = dv.float().sum(2), do.float().sum(2)
-    assert (dvs - dos).abs().max().item() < 0.05 * max(1.0, dos.abs().max().item())
+    dv_l1 = dv.float().abs().sum(2)
+    assert ((dvs - dos).abs() <= 0.02 * dv_l1 + 1e-2).all(), ((dvs - dos).abs() / dv_l1).max().item()
     for (b, h) in samples:
         sl = [t[b, h].float().cpu().numpy()[None] for t in (q, k, v, do)]
         ro, _ = ora.attn_fwd(*sl[:3], scale, causal)
