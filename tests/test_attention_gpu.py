@@ -94,7 +94,9 @@ def test_bf16_paths_agree_with_simt(causal):
         outs.append([o.float(), lse] + [t.float() for t in g])
     ctx.force_simt(False)
     for a, b in zip(*outs):
-        assert (a - b).abs().max().item() < 2e-2
+        a, b = a.cpu().numpy(), b.cpu().numpy()
+        # both sides are bf16-rounded: allow 2e-2 or two bf16 spacings
+        assert (np.abs(a - b) <= 2 * _bf16_tol(b, 1e-2)).all(), np.abs(a - b).max()
 
 
 def test_strided_bshd_layout_matches_contiguous():
