@@ -77,6 +77,8 @@ SIGNATURES = {
     "hx_attn_bwd_workspace_size": (_I, [_I, _SHP, ctypes.POINTER(_U64)]),
     "hx_flash_attention_bwd": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _U64,
                                     _I, _I, _I, _F, _I]),
+    "hx_flash_attention_bwd_noalloc": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                            _I, _I, _I, _F, _I]),
     "hx_attn_fwd_strided": (_I, [_P, _I, _SHP, _P, _P, _P, _P, _P, _F, _I]),
     "hx_attn_bwd_strided": (_I, [_P, _I, _SHP, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _U64,
                                  _F, _I]),

@@ -145,6 +145,22 @@ int hx_flash_attention_bwd(hx_ctx* ctx, hx_dtype dtype, const void* q, const voi
                            uint64_t workspace_bytes, int bh, int seq_len, int head_dim,
                            float scale, int causal);
 
+/* Same result as hx_flash_attention_bwd, but allocates no device memory: the
+ * workspace lives in a fixed 64 MiB array compiled into the library (held on
+ * every GPU that loads it until the process exits). No counterpart in the
+ * reference; it exists for callers that cannot let a library allocate (a
+ * runtime that gave all device memory to its own pool, a loop that cannot
+ * afford cudaMalloc's synchronisation, an operator callback that must not
+ * allocate). bf16 with head_dim 64 or 128 only. Problems whose workspace
+ * (hx_attn_bwd_workspace_size) exceeds 64 MiB return HX_ERR_INVALID. Calls
+ * share the array: calls that overlap on the GPU race, so serialize them.
+ * The first call on a device resolves the array's address; make it before
+ * any stream capture. */
+int hx_flash_attention_bwd_noalloc(hx_ctx* ctx, hx_dtype dtype, const void* q, const void* k,
+                                   const void* v, const void* o, const void* dout,
+                                   const float* lse, void* dq, void* dk, void* dv, int bh,
+                                   int seq_len, int head_dim, float scale, int causal);
+
 /* ---- fused attention on strided [B, H, S, D] views ------------------------- */
 /* lse is contiguous [B, H, S]. */
 int hx_attn_fwd_strided(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape, const void* q,
