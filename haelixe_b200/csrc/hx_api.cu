@@ -183,6 +183,8 @@ int hx_ctx_destroy(hx_ctx* c) {
         c->arena.live.clear();
         cudaStreamSynchronize(c->own_stream);
     }
+    for (auto& t : c->rope_tables) cudaFree(t.tab);
+    c->rope_tables.clear();
     if (c->arena.pool) cudaMemPoolDestroy(c->arena.pool);
     if (c->status) cudaFree(c->status);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
@@ -480,15 +482,40 @@ static int rope_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const
     if ((st = validate_dtype(c, dt, who)) || (st = validate_shape(c, shape, who))) return st;
     if (!x || !out) return set_error(c, HX_ERR_INVALID, "%s: NULL operand", who);
     if (shape->D % 2) return set_error(c, HX_ERR_INVALID, "%s: head_dim must be even", who);
-    // base^(-(2i)/D) in f32, the reference's expression (src/kernels/rope.rs:27-28).
-    float inv_freq[128];
-    for (int i = 0; i < shape->D / 2; ++i) {
-        const float exponent = -((float)(2 * i)) / (float)shape->D;
-        inv_freq[i] = powf(base, exponent);
-    }
+    if (!isfinite(base) || base <= 0.f)
+        return set_error(c, HX_ERR_INVALID, "%s: base must be positive and finite", who);
     DeviceGuard g(c->device);
     LaunchCount lc(c);
-    return check_cuda(c, hx::rope_apply(c->stream, dt, hx::dims_of(*shape), x, out, inv_freq, sign),
+    uint32_t base_bits;
+    memcpy(&base_bits, &base, 4);
+    float2* tab = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(c->rope_mu);
+        for (const auto& t : c->rope_tables)
+            if (t.S == shape->S && t.D == shape->D && t.base_bits == base_bits) tab = t.tab;
+        if (tab == nullptr) {
+            // base^(-(2i)/D) in f32, the reference's expression (src/kernels/rope.rs:27-28).
+            float inv_freq[128];
+            for (int i = 0; i < shape->D / 2; ++i) {
+                const float exponent = -((float)(2 * i)) / (float)shape->D;
+                inv_freq[i] = powf(base, exponent);
+            }
+            if ((st = check_cuda(c, cudaMalloc(&tab, sizeof(float2) * (size_t)shape->S * (shape->D / 2)),
+                                 "cudaMalloc(rope table)")))
+                return st;
+            if ((st = check_cuda(c, hx::rope_table(c->stream, shape->S, shape->D, inv_freq, tab), who))) {
+                cudaFree(tab);
+                return st;
+            }
+            // One-time: later calls may come on other streams.
+            if ((st = check_cuda(c, cudaStreamSynchronize(c->stream), "cudaStreamSynchronize"))) {
+                cudaFree(tab);
+                return st;
+            }
+            c->rope_tables.push_back({shape->S, shape->D, base_bits, tab});
+        }
+    }
+    return check_cuda(c, hx::rope_apply(c->stream, c->sm_count, dt, hx::dims_of(*shape), x, out, tab, sign),
                       who);
 }
 

@@ -23,6 +23,12 @@ struct DeviceStatus {
     int pad;
 };
 
+struct RopeTable {
+    int S, D;
+    uint32_t base_bits;
+    float2* tab;  // device, [S][D/2]
+};
+
 struct Arena {
     cudaMemPool_t pool = nullptr;
     std::mutex mu;
@@ -45,6 +51,8 @@ struct hx_ctx {
     int force_simt = 0;
     mutable std::mutex err_mu;
     std::string last_error;
+    std::mutex rope_mu;
+    std::vector<hx::RopeTable> rope_tables;  // (cos, sin) tables, freed with the context
 };
 
 namespace hx {
@@ -92,7 +100,9 @@ void note_launch();
 uint64_t launches_of_this_thread();
 
 // ---- RoPE (rope.cu) ----
-cudaError_t rope_apply(cudaStream_t st, hx_dtype dt, const AttnDims& d, const void* x, void* out,
-                       const float* inv_freq_host, float sign);
+// Fills tab[S][D/2] with (cos, sin) of s * inv_freq[i].
+cudaError_t rope_table(cudaStream_t st, int S, int D, const float* inv_freq_host, float2* tab);
+cudaError_t rope_apply(cudaStream_t st, int sm_count, hx_dtype dt, const AttnDims& d,
+                       const void* x, void* out, const float2* tab, float sign);
 
 }  // namespace hx
