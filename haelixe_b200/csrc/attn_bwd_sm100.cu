@@ -39,13 +39,22 @@ using namespace ptx;
 
 constexpr int BK = 128;  // keys per CTA (UMMA M of S^T, dP^T, dV, dK)
 constexpr int kThreads = 384;
+// Register split (setmaxnreg) per SM sub-partition, one warp of each group:
+// control 56 + P/dS 256 + dQ drain 192 = 504 = 3 x 168 (the launch count,
+// checked on the host before every launch).
+constexpr int kRegsLaunch = 168;
+constexpr int kRegsCtl = 56;
+constexpr int kRegsCompute = 256;
+constexpr int kRegsDrain = 192;
+static_assert(kRegsCtl + kRegsCompute + kRegsDrain == 3 * kRegsLaunch, "register split");
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
 struct BCfg {
     static constexpr int BQ = D == 128 ? 64 : 128;  // queries per inner tile
     static constexpr bool DQ_T = D == 128;           // dQ computed transposed (M = D)
-    static constexpr int QST = 2;                    // Q/dO ring depth
+    static constexpr int QST = 3;                    // Q/dO/lse/delta ring depth
+    static_assert(QST <= 4, "BBars holds 4 ring stages");
     static constexpr int CHUNK_K = BK * 128;         // bytes of a 64-column chunk of a K/V tile
     static constexpr int CHUNK_Q = BQ * 128;         // ... of a Q/dO tile
     static constexpr int CHUNK_DS = BK * 128;        // ... of the dS^T tile (64 queries wide)
@@ -57,31 +66,37 @@ struct BCfg {
     static constexpr int Q_OFF = V_OFF + KT;
     static constexpr int DO_OFF = Q_OFF + QST * QT;
     static constexpr int DS_OFF = DO_OFF + QST * QT;
-    static constexpr int LSE_OFF = DS_OFF + DST;
+    static constexpr int DQS = BQ * D * 4;           // f32 dQ staging tile for the reduce-add
+    static constexpr int DQS_OFF = DS_OFF + DST;
+    static constexpr int LSE_OFF = DQS_OFF + DQS;
     static constexpr int DEL_OFF = LSE_OFF + QST * BQ * 4;
     static constexpr int BAR_OFF = DEL_OFF + QST * BQ * 4;
     static constexpr int SMEM = BAR_OFF + 256 + 1024;
-    // TMEM columns
+    // TMEM columns. D=128: two S^T buffers (the next tile's K Q^T runs while P of
+    // this one is computed) and one dQ^T buffer; D=64: one S^T buffer, two dQ.
+    static constexpr int NSB = D == 128 ? 2 : 1;
+    static constexpr int NDQ = D == 128 ? 1 : 2;
     static constexpr int DQ_COLS = DQ_T ? BQ : D;
-    static constexpr uint32_t C_S = 0, C_DP = BQ, C_DQ0 = 2 * BQ, C_DQ1 = 2 * BQ + DQ_COLS,
-                              C_DV = 2 * BQ + 2 * DQ_COLS, C_DK = C_DV + D;
+    static constexpr uint32_t C_S0 = 0, C_DP = NSB * BQ, C_DQ0 = C_DP + BQ,
+                              C_DV = C_DQ0 + NDQ * DQ_COLS, C_DK = C_DV + D;
     static_assert(C_DK + D <= 512, "TMEM budget");
 };
 
 struct BBars {
     uint64_t kv_full;
-    uint64_t q_full[2], q_empty[2];
-    uint64_t s_full, dp_full, p_full, ds_full;
+    uint64_t q_full[4], q_empty[4];  // indexed by ring stage (QST <= 4)
+    uint64_t s_full[2], dp_full, p_full, ds_full;
     uint64_t dq_full[2], dq_empty[2];
+    uint64_t dqs_free, dqs_full;
     uint64_t acc_done, done;
     uint32_t tmem_base;
     int abort_flag;
 };
 
 struct BwdParams {
-    const float* lse;    // [B,H,S]
-    const float* delta;  // [B,H,S]
-    float* dq_acc;       // [B,H,S,D] f32
+    const float* lse2;   // [B*H][S_pad]: lse * log2(e), 0 past S
+    const float* delta;  // [B*H][S_pad]: rowsum(dO * O), 0 past S
+    int S_pad;
     __nv_bfloat16* dk;
     __nv_bfloat16* dv;
     int64_t sb, sh, ss;  // strides of dk/dv (elements)
@@ -103,7 +118,7 @@ template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                    const BwdParams p) {
+                    const __grid_constant__ CUtensorMap tdq, const BwdParams p) {
     using C = BCfg<D>;
     constexpr int BQ = C::BQ;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -123,10 +138,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         bars->abort_flag = 0;
         mbar_init(bar_addr(bars->kv_full), 1);
         for (int s = 0; s < C::QST; ++s) {
-            mbar_init(bar_addr(bars->q_full[s]), 1 + 32);
+            mbar_init(bar_addr(bars->q_full[s]), 1);
             mbar_init(bar_addr(bars->q_empty[s]), 1);
         }
-        mbar_init(bar_addr(bars->s_full), 1);
+        mbar_init(bar_addr(bars->s_full[0]), 1);
+        mbar_init(bar_addr(bars->s_full[1]), 1);
         mbar_init(bar_addr(bars->dp_full), 1);
         mbar_init(bar_addr(bars->p_full), 128);
         mbar_init(bar_addr(bars->ds_full), 128);
@@ -134,6 +150,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(bar_addr(bars->dq_full[s]), 1);
             mbar_init(bar_addr(bars->dq_empty[s]), 128);
         }
+        mbar_init(bar_addr(bars->dqs_free), 1);
+        mbar_init(bar_addr(bars->dqs_full), 128);
         mbar_init(bar_addr(bars->acc_done), 1);
         mbar_init(bar_addr(bars->done), 1);
         fence_mbar_init();
@@ -148,11 +166,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tk);
         prefetch_tmap(&tv);
         prefetch_tmap(&tdo);
+        prefetch_tmap(&tdq);
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
+    if (warp < 4) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegsCtl));
+    } else if (warp < 8) {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsCompute));
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsDrain));
+    }
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -165,37 +191,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         int issued = 0;
-        for (int it = 0; it < n_it; ++it) {
-            const int st = it % C::QST;
-            const uint32_t ph = (it / C::QST) & 1;
-            const int q0 = (i_start + it) * BQ;
-            if (!mbar_wait(bar_addr(bars->q_empty[st]), ph ^ 1, abort_flag, p.status, 40)) break;
-            const uint32_t qb = bar_addr(bars->q_full[st]);
-            if (lane == 0) {
-                mbar_arrive_expect_tx(qb, 2 * C::QT);
+        if (lane == 0) {
+            for (int it = 0; it < n_it; ++it) {
+                const int st = it % C::QST;
+                const uint32_t ph = (it / C::QST) & 1;
+                const int q0 = (i_start + it) * BQ;
+                if (!mbar_wait(bar_addr(bars->q_empty[st]), ph ^ 1, abort_flag, p.status, 40)) break;
+                const uint32_t qb = bar_addr(bars->q_full[st]);
+                mbar_arrive_expect_tx(qb, 2 * C::QT + 2 * BQ * 4);
                 for (int c = 0; c < D / 64; ++c) {
                     tma_load_4d(smem_addr(sm + C::Q_OFF + st * C::QT + c * C::CHUNK_Q), &tq, qb,
                                 c * 64, q0, h, b);
                     tma_load_4d(smem_addr(sm + C::DO_OFF + st * C::QT + c * C::CHUNK_Q), &tdo, qb,
                                 c * 64, q0, h, b);
                 }
+                const int64_t row0 = bh * p.S_pad + q0;
+                bulk_load(smem_addr(s_lse + st * BQ), p.lse2 + row0, BQ * 4, qb);
+                bulk_load(smem_addr(s_del + st * BQ), p.delta + row0, BQ * 4, qb);
+                issued = it + 1;
             }
-            for (int i = lane; i < BQ; i += 32) {
-                const int q = q0 + i;
-                s_lse[st * BQ + i] = q < p.S ? p.lse[bh * p.S + q] * kLog2e : 0.f;
-                s_del[st * BQ + i] = q < p.S ? p.delta[bh * p.S + q] : 0.f;
-            }
-            mbar_arrive(qb);
-            issued = it + 1;
-        }
-        if (lane == 0) {
             mbar_wait_drain(kvb, 0);
             for (int it = max(0, issued - C::QST); it < issued; ++it)
                 mbar_wait_drain(bar_addr(bars->q_full[it % C::QST]), (it / C::QST) & 1);
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        // Teardown stays inside each role branch: no code is shared across the
+        // register split.
+        __syncwarp();
+        tc_fence_before();
+        __syncthreads();
+    } else if (warp < 4) {
+        // ------------------------------------------------------------ MMA issuer (warp 1, lane 0)
+        if (warp == 1 && lane == 0) {
             constexpr uint32_t idSP = idesc_bf16_f32(BK, BQ, false, false);
             constexpr uint32_t idAcc = idesc_bf16_f32(BK, D, false, true);
             constexpr uint32_t idDQ =
@@ -231,50 +257,77 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 sdesc_sw128(sK + kk * 2048, C::CHUNK_K, 1024), idDQ, kk > 0);
                 }
             };
-            bool ok = mbar_wait(bar_addr(bars->kv_full), 0, abort_flag, p.status, 50) &&
-                      mbar_wait(bar_addr(bars->q_full[0]), 0, abort_flag, p.status, 51);
+            auto s_col = [&](int it) { return C::C_S0 + (uint32_t)((it % C::NSB) * BQ); };
+            auto q_wait = [&](int it) {
+                return mbar_wait(bar_addr(bars->q_full[it % C::QST]), (it / C::QST) & 1, abort_flag,
+                                 p.status, 51);
+            };
+            auto issue_s = [&](int it) {
+                issue_sp(s_col(it), sK, sQ + (it % C::QST) * C::QT);
+                umma_commit(bar_addr(bars->s_full[it % C::NSB]));
+            };
+            bool ok = mbar_wait(bar_addr(bars->kv_full), 0, abort_flag, p.status, 50) && q_wait(0);
             if (ok) {
                 tc_fence_after();
-                issue_sp(C::C_S, sK, sQ);
-                umma_commit(bar_addr(bars->s_full));
-                issue_sp(C::C_DP, sV, sDO);
-                umma_commit(bar_addr(bars->dp_full));
+                issue_s(0);
+                if (C::NSB == 2 && n_it > 1) {
+                    ok = q_wait(1);
+                    if (ok) {
+                        tc_fence_after();
+                        issue_s(1);
+                    }
+                }
+                if (ok) {
+                    issue_sp(C::C_DP, sV, sDO);
+                    umma_commit(bar_addr(bars->dp_full));
+                }
             }
             for (int it = 0; ok && it < n_it; ++it) {
                 const int st = it % C::QST;
-                const int stn = (it + 1) % C::QST;
-                const uint32_t phn = ((it + 1) / C::QST) & 1;
                 if (!(ok = mbar_wait(bar_addr(bars->p_full), it & 1, abort_flag, p.status, 52))) break;
                 tc_fence_after();
-                issue_acc(C::C_DV, C::C_S, sDO + st * C::QT, it == 0);
-                if (it + 1 < n_it) {
-                    if (!(ok = mbar_wait(bar_addr(bars->q_full[stn]), phn, abort_flag, p.status, 53)))
-                        break;
+                issue_acc(C::C_DV, s_col(it), sDO + st * C::QT, it == 0);
+                if (C::NSB == 1 && it + 1 < n_it) {
+                    // The single S^T buffer is free once dV(it) (issued above) has read P^T(it).
+                    if (!(ok = q_wait(it + 1))) break;
                     tc_fence_after();
-                    issue_sp(C::C_S, sK, sQ + stn * C::QT);
-                    umma_commit(bar_addr(bars->s_full));
+                    issue_s(it + 1);
                 }
                 if (!(ok = mbar_wait(bar_addr(bars->ds_full), it & 1, abort_flag, p.status, 54))) break;
                 tc_fence_after();
                 issue_acc(C::C_DK, C::C_DP, sQ + st * C::QT, it == 0);
-                const int buf = it & 1;
-                if (!(ok = mbar_wait(bar_addr(bars->dq_empty[buf]), ((it >> 1) & 1) ^ 1, abort_flag,
-                                     p.status, 55)))
+                const int dqb = it % C::NDQ;
+                if (!(ok = mbar_wait(bar_addr(bars->dq_empty[dqb]), ((it / C::NDQ) & 1) ^ 1,
+                                     abort_flag, p.status, 55)))
                     break;
                 tc_fence_after();
-                issue_dq(buf ? C::C_DQ1 : C::C_DQ0);
-                umma_commit(bar_addr(bars->dq_full[buf]));
+                issue_dq(C::C_DQ0 + (uint32_t)(dqb * C::DQ_COLS));
+                umma_commit(bar_addr(bars->dq_full[dqb]));
                 umma_commit(bar_addr(bars->q_empty[st]));
                 if (it + 1 < n_it) {
-                    issue_sp(C::C_DP, sV, sDO + stn * C::QT);
+                    // dO(it+1) landed with Q(it+1), waited for when S^T(it+1) was issued.
+                    issue_sp(C::C_DP, sV, sDO + ((it + 1) % C::QST) * C::QT);
                     umma_commit(bar_addr(bars->dp_full));
+                }
+                if (C::NSB == 2 && it + 2 < n_it) {
+                    // S^T buffer of tile it is free: dV(it) read its P^T, in issue order.
+                    if (!(ok = q_wait(it + 2))) break;
+                    tc_fence_after();
+                    issue_s(it + 2);
                 }
             }
             umma_commit(bar_addr(bars->acc_done));
             umma_commit(bar_addr(bars->done));
             mbar_wait_drain(bar_addr(bars->done), 0);
         }
-    } else if (warp >= 4 && warp < 8) {
+        __syncwarp();
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 2) {  // warp 2 allocated the TMEM; it frees it once every role is done
+            tc_fence_after();
+            tmem_dealloc(tmem, 512);
+        }
+    } else if (warp < 8) {
         // ------------------------------------------------------------ P / dS warpgroup
         const int wi = warp % 4;
         const int r = wi * 32 + lane;  // key row within the tile (TMEM lane)
@@ -283,47 +336,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sl2 = p.scale * kLog2e;
         uint8_t* ds_row = sm + C::DS_OFF + r * 128;
         bool ok = true;
+        // P and dS stay in registers between the two phases: f32 when BQ = 64,
+        // packed bf16 when BQ = 128 (register budget).
+        constexpr bool kKeepF32 = BQ == 64;
+        constexpr int CHK = 64;  // columns per TMEM load batch
         for (int it = 0; it < n_it; ++it) {
             const int st = it % C::QST;
             const uint32_t ph = (it / C::QST) & 1;
             const int q0 = (i_start + it) * BQ;
+            const uint32_t cS = C::C_S0 + (uint32_t)((it % C::NSB) * BQ);
             if (!(ok = mbar_wait(bar_addr(bars->q_full[st]), ph, abort_flag, p.status, 60))) break;
-            if (!(ok = mbar_wait(bar_addr(bars->s_full), it & 1, abort_flag, p.status, 61))) break;
+            if (!(ok = mbar_wait(bar_addr(bars->s_full[it % C::NSB]), (it / C::NSB) & 1, abort_flag,
+                                 p.status, 61)))
+                break;
             tc_fence_after();
             const float* lse2 = s_lse + st * BQ;
             const float* del = s_del + st * BQ;
             const bool need_mask = (q0 + BQ > p.S) || (k0 + BK > p.S) || (p.causal && k0 + BK - 1 > q0);
-            // P^T = exp2(S^T * scale*log2e - lse*log2e), 32 columns at a time. The
-            // packed P of chunk c lands on S columns [c/2, c/2+16), all already read.
-            // P stays in registers for dS: f32 when BQ = 64, packed bf16 when BQ = 128.
-            constexpr bool kKeepF32 = BQ == 64;
+            // P^T = exp2(S^T * scale*log2e - lse*log2e). Each 64-column batch is loaded
+            // with one wait; its packed P lands on S columns [c/2, c/2+32), already read.
             float pr[kKeepF32 ? BQ : 1];
             uint32_t pkeep[kKeepF32 ? 1 : BQ / 2];
 #pragma unroll
-            for (int c = 0; c < BQ; c += 32) {
-                uint32_t x[32];
-                tmem_ld32(tl + C::C_S + c, x);
+            for (int c = 0; c < BQ; c += CHK) {
+                uint32_t x[CHK];
+                tmem_ld32(tl + cS + c, x);
+                tmem_ld32(tl + cS + c + 32, x + 32);
                 tmem_ld_wait();
-                reg_fence<32>(x);
-                uint32_t pk[16];
+                reg_fence<CHK>(x);
+                uint32_t pk[CHK / 2];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    float p0 = ex2(fmaf(__uint_as_float(x[2 * i]), sl2, -lse2[c + 2 * i]));
-                    float p1 = ex2(fmaf(__uint_as_float(x[2 * i + 1]), sl2, -lse2[c + 2 * i + 1]));
-                    if (need_mask) {
-                        const int qa = q0 + c + 2 * i, qb = qa + 1;
-                        p0 = (qa < p.S && kr < p.S && (!p.causal || kr <= qa)) ? p0 : 0.f;
-                        p1 = (qb < p.S && kr < p.S && (!p.causal || kr <= qb)) ? p1 : 0.f;
-                    }
-                    pk[i] = pack_bf16(p0, p1);
-                    if constexpr (kKeepF32) {
-                        pr[c + 2 * i] = p0;
-                        pr[c + 2 * i + 1] = p1;
-                    } else {
-                        pkeep[c / 2 + i] = pk[i];
+                for (int g = 0; g < CHK / 4; ++g) {
+                    const float4 l4 = reinterpret_cast<const float4*>(lse2 + c)[g];
+                    const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; e += 2) {
+                        const int i = 4 * g + e;
+                        float p0 = ex2(fmaf(__uint_as_float(x[i]), sl2, -lv[e]));
+                        float p1 = ex2(fmaf(__uint_as_float(x[i + 1]), sl2, -lv[e + 1]));
+                        if (need_mask) {
+                            const int qa = q0 + c + i, qb = qa + 1;
+                            p0 = (qa < p.S && kr < p.S && (!p.causal || kr <= qa)) ? p0 : 0.f;
+                            p1 = (qb < p.S && kr < p.S && (!p.causal || kr <= qb)) ? p1 : 0.f;
+                        }
+                        pk[i / 2] = pack_bf16(p0, p1);
+                        if constexpr (kKeepF32) {
+                            pr[c + i] = p0;
+                            pr[c + i + 1] = p1;
+                        } else {
+                            pkeep[(c + i) / 2] = pk[i / 2];
+                        }
                     }
                 }
-                tmem_st16(tl + C::C_S + c / 2, pk);
+                tmem_st32(tl + cS + c / 2, pk);
             }
             tmem_st_wait();
             tc_fence_before();
@@ -331,37 +396,42 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             if (!(ok = mbar_wait(bar_addr(bars->dp_full), it & 1, abort_flag, p.status, 62))) break;
             tc_fence_after();
-            // dS^T = P^T (dP^T - delta) -> TMEM (over dP, same chunk argument) and the
+            // dS^T = P^T (dP^T - delta) -> TMEM (over dP, same batch argument) and the
             // 128-byte-swizzled smem tile read by the dQ MMA.
 #pragma unroll
-            for (int c = 0; c < BQ; c += 32) {
-                uint32_t x[32];
+            for (int c = 0; c < BQ; c += CHK) {
+                uint32_t x[CHK];
                 tmem_ld32(tl + C::C_DP + c, x);
+                tmem_ld32(tl + C::C_DP + c + 32, x + 32);
                 tmem_ld_wait();
-                reg_fence<32>(x);
-                uint32_t dk[16];
+                reg_fence<CHK>(x);
+                uint32_t dk[CHK / 2];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    float p0, p1;
-                    if constexpr (kKeepF32) {
-                        p0 = pr[c + 2 * i];
-                        p1 = pr[c + 2 * i + 1];
-                    } else {
-                        p0 = __uint_as_float(pkeep[c / 2 + i] << 16);
-                        p1 = __uint_as_float(pkeep[c / 2 + i] & 0xffff0000u);
+                for (int g = 0; g < CHK / 4; ++g) {
+                    const float4 d4 = reinterpret_cast<const float4*>(del + c)[g];
+                    const float dl[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; e += 2) {
+                        const int i = 4 * g + e;
+                        float p0, p1;
+                        if constexpr (kKeepF32) {
+                            p0 = pr[c + i];
+                            p1 = pr[c + i + 1];
+                        } else {
+                            p0 = __uint_as_float(pkeep[(c + i) / 2] << 16);
+                            p1 = __uint_as_float(pkeep[(c + i) / 2] & 0xffff0000u);
+                        }
+                        const float d0 = p0 * (__uint_as_float(x[i]) - dl[e]);
+                        const float d1 = p1 * (__uint_as_float(x[i + 1]) - dl[e + 1]);
+                        dk[i / 2] = pack_bf16(d0, d1);
                     }
-                    const float d0 = p0 * (__uint_as_float(x[2 * i]) - del[c + 2 * i]);
-                    const float d1 = p1 * (__uint_as_float(x[2 * i + 1]) - del[c + 2 * i + 1]);
-                    dk[i] = pack_bf16(d0, d1);
                 }
-                tmem_st16(tl + C::C_DP + c / 2, dk);
+                tmem_st32(tl + C::C_DP + c / 2, dk);
                 uint8_t* chunk_row = ds_row + (c / 64) * C::CHUNK_DS;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int u = (c % 64) / 8 + j;
+                for (int u = 0; u < 8; ++u)
                     *reinterpret_cast<uint4*>(chunk_row + ((u ^ (r & 7)) * 16)) =
-                        make_uint4(dk[4 * j], dk[4 * j + 1], dk[4 * j + 2], dk[4 * j + 3]);
-                }
+                        make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
             }
             tmem_st_wait();
             fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
@@ -399,61 +469,96 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else if (warp >= 8) {
+        tc_fence_before();
+        __syncthreads();
+    } else {
         // ------------------------------------------------------------ dQ drain warpgroup
+        // Each dQ tile goes TMEM -> registers -> f32 staging tile in smem, and one
+        // thread adds the tile into the accumulator with a bulk tensor reduce-add
+        // (the TMA unit does the read-modify-write in L2; no per-element atomics).
         const int wi = warp % 4;
         const int r = wi * 32 + lane;  // TMEM lane: d (dQ^T) or query row (dQ)
         const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
+        const bool elected = (warp == 8 && lane == 0);
+        float* stage = (float*)(sm + C::DQS_OFF);
         for (int it = 0; it < n_it; ++it) {
-            const int buf = it & 1;
+            const int buf = it % C::NDQ;
             const int q0 = (i_start + it) * BQ;
-            if (!mbar_wait(bar_addr(bars->dq_full[buf]), (it >> 1) & 1, abort_flag, p.status, 70)) break;
+            if (!mbar_wait(bar_addr(bars->dq_full[buf]), (it / C::NDQ) & 1, abort_flag, p.status, 70)) break;
             tc_fence_after();
             uint32_t v[C::DQ_COLS];
-            tmem_ld_cols<C::DQ_COLS>(tl + (buf ? C::C_DQ1 : C::C_DQ0), v);
+            tmem_ld_cols<C::DQ_COLS>(tl + C::C_DQ0 + (uint32_t)(buf * C::DQ_COLS), v);
             tmem_ld_wait();
             reg_fence<C::DQ_COLS>(v);
             tc_fence_before();
             mbar_arrive(bar_addr(bars->dq_empty[buf]));
+            // The previous reduce-add must have read the staging tile.
+            if (elected) {
+                bulk_wait_group_read0();
+                mbar_arrive(bar_addr(bars->dqs_free));
+            }
+            if (!mbar_wait(bar_addr(bars->dqs_free), it & 1, abort_flag, p.status, 71)) break;
             if (C::DQ_T) {
-                // lane r = d; column c = query q0 + c: a warp adds 32 consecutive floats.
-                float* base = p.dq_acc + (bh * p.S + q0) * D + r;
+                // staging [BQ queries][D] row-major: lane r = d, a warp writes 32 consecutive floats.
 #pragma unroll
-                for (int c = 0; c < BQ; ++c)
-                    if (q0 + c < p.S) atomicAdd(base + (int64_t)c * D, __uint_as_float(v[c]));
+                for (int c = 0; c < BQ; ++c) stage[c * D + r] = __uint_as_float(v[c]);
             } else {
-                const int q = q0 + r;
-                if (q < p.S) {
-                    float4* row = reinterpret_cast<float4*>(p.dq_acc + (bh * p.S + q) * D);
+                // staging = two 128B-swizzled boxes [BQ rows][32 floats]; lane r = query row.
 #pragma unroll
-                    for (int c = 0; c < D; c += 4)
-                        atomicAdd(row + c / 4, make_float4(__uint_as_float(v[c]), __uint_as_float(v[c + 1]),
-                                                           __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3])));
+                for (int cb = 0; cb < D / 32; ++cb) {
+                    uint8_t* row = (uint8_t*)stage + cb * (BQ * 128) + r * 128;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) * 16)) =
+                            make_uint4(v[cb * 32 + 4 * j], v[cb * 32 + 4 * j + 1],
+                                       v[cb * 32 + 4 * j + 2], v[cb * 32 + 4 * j + 3]);
                 }
             }
+            fence_proxy_async();
+            mbar_arrive(bar_addr(bars->dqs_full));
+            if (elected) {
+                if (!mbar_wait(bar_addr(bars->dqs_full), it & 1, abort_flag, p.status, 72)) break;
+                if (C::DQ_T) {
+                    tma_reduce_add_3d(&tdq, smem_addr(stage), 0, q0, (int)bh);
+                } else {
+#pragma unroll
+                    for (int cb = 0; cb < D / 32; ++cb)
+                        tma_reduce_add_3d(&tdq, smem_addr((uint8_t*)stage + cb * (BQ * 128)), cb * 32,
+                                          q0, (int)bh);
+                }
+                bulk_commit_group();
+            }
         }
-    }
-
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 2) {
-        tc_fence_after();
-        tmem_dealloc(tmem, 512);
+        if (elected) bulk_wait_group0();
+        tc_fence_before();
+        __syncthreads();
     }
 }
 
-// delta = rowsum(dO * O) in f32; also zeroes the row of the dQ accumulator.
+// Per row (b, h, s) of the padded [B*H][S_pad] tables: lse2 = lse * log2(e)
+// and delta = rowsum(dO * O) in f32 (0 for s >= S), and zero the row of the
+// dQ accumulator. One warp per row.
 template <int D>
 __global__ void __launch_bounds__(256) bwd_pre_kernel(const __nv_bfloat16* __restrict__ o,
                                                       const __nv_bfloat16* __restrict__ dout,
+                                                      const float* __restrict__ lse,
+                                                      float* __restrict__ lse2,
                                                       float* __restrict__ delta,
-                                                      float* __restrict__ dq_acc, AttnDims d) {
-    const int64_t rows = (int64_t)d.B * d.H * d.S;
+                                                      float* __restrict__ dq_acc, AttnDims d,
+                                                      int S_pad) {
+    const int64_t rows = (int64_t)d.B * d.H * S_pad;
     const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
     const int lane = threadIdx.x % 32;
     if (r >= rows) return;
-    const int s = (int)(r % d.S);
-    const int64_t bhi = r / d.S;
+    const int s = (int)(r % S_pad);
+    const int64_t bhi = r / S_pad;
+    if (s >= d.S) {
+        if (lane == 0) {
+            lse2[r] = 0.f;
+            delta[r] = 0.f;
+        }
+        return;
+    }
     const int hi = (int)(bhi % d.H), bi = (int)(bhi / d.H);
     const int64_t off = (int64_t)bi * d.sb + (int64_t)hi * d.sh + (int64_t)s * d.ss;
     constexpr int PER = D / 32;  // elements per lane (2 or 4)
@@ -476,8 +581,11 @@ __global__ void __launch_bounds__(256) bwd_pre_kernel(const __nv_bfloat16* __res
     }
 #pragma unroll
     for (int w = 16; w > 0; w >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, w);
-    if (lane == 0) delta[r] = acc;
-    float4* z = reinterpret_cast<float4*>(dq_acc + r * D);
+    if (lane == 0) {
+        delta[r] = acc;
+        lse2[r] = lse[bhi * d.S + s] * kLog2e;
+    }
+    float4* z = reinterpret_cast<float4*>(dq_acc + (bhi * d.S + s) * D);
     for (int i = lane; i < D / 4; i += 32) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
@@ -508,34 +616,70 @@ __global__ void __launch_bounds__(256) bwd_post_kernel(const float* __restrict__
 
 uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
 
+// Workspace: lse2 [B*H][S_pad] | delta [B*H][S_pad] | dQ accumulator [B*H][S][D] (f32).
+struct BwdWorkspace {
+    float* lse2;
+    float* delta;
+    float* dq_acc;
+    int S_pad;
+};
+
+BwdWorkspace carve(void* ws, const AttnDims& d) {
+    const int S_pad = (d.S + 127) / 128 * 128;
+    const uint64_t tab = align256((uint64_t)d.B * d.H * S_pad * 4);
+    BwdWorkspace w;
+    w.lse2 = (float*)ws;
+    w.delta = (float*)((uint8_t*)ws + tab);
+    w.dq_acc = (float*)((uint8_t*)ws + 2 * tab);
+    w.S_pad = S_pad;
+    return w;
+}
+
 template <int D>
 cudaError_t launch(cudaStream_t st, int sm_count, DeviceStatus* status, const AttnDims& d,
                    const void* q, const void* k, const void* v, const void* o, const void* dout,
                    const float* lse, void* dq, void* dk, void* dv, void* ws, float scale,
                    int causal) {
     using C = BCfg<D>;
-    const int64_t rows = (int64_t)d.B * d.H * d.S;
-    float* delta = (float*)ws;
-    float* dq_acc = (float*)((uint8_t*)ws + align256((uint64_t)rows * 4));
-    bwd_pre_kernel<D><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(
-        (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, delta, dq_acc, d);
+    const BwdWorkspace w = carve(ws, d);
+    const int64_t rows_pad = (int64_t)d.B * d.H * w.S_pad;
+    bwd_pre_kernel<D><<<(unsigned)((rows_pad * 32 + 255) / 256), 256, 0, st>>>(
+        (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, lse, w.lse2, w.delta, w.dq_acc, d,
+        w.S_pad);
     note_launch();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
 
-    CUtensorMap tq, tk, tv, tdo;
+    CUtensorMap tq, tk, tv, tdo, tdq;
     if (!make_tmap_bhsd(&tq, q, d.B, d.H, d.S, D, d.sb, d.sh, d.ss, 64, C::BQ) ||
         !make_tmap_bhsd(&tdo, dout, d.B, d.H, d.S, D, d.sb, d.sh, d.ss, 64, C::BQ) ||
         !make_tmap_bhsd(&tk, k, d.B, d.H, d.S, D, d.sb, d.sh, d.ss, 64, BK) ||
         !make_tmap_bhsd(&tv, v, d.B, d.H, d.S, D, d.sb, d.sh, d.ss, 64, BK))
         return cudaErrorInvalidValue;
+    // dQ accumulator [B*H][S][D] f32: D=128 tiles are [BQ][128] plain, D=64 tiles are
+    // two [BQ][32] boxes with 128-byte swizzle (matches the staging writes).
+    const bool ok_dq = C::DQ_T
+        ? make_tmap_f32_3d(&tdq, w.dq_acc, D, d.S, (uint64_t)d.B * d.H, D, C::BQ, false)
+        : make_tmap_f32_3d(&tdq, w.dq_acc, D, d.S, (uint64_t)d.B * d.H, 32, C::BQ, true);
+    if (!ok_dq) return cudaErrorInvalidValue;
+    // setmaxnreg.inc waits until the warp's share fits the block's launch
+    // allocation: launch only with exactly the register count the split assumes.
+    {
+        static int regs = -1;
+        if (regs < 0) {
+            cudaFuncAttributes fa;
+            if (cudaFuncGetAttributes(&fa, attn_bwd_kernel<D>) != cudaSuccess) return cudaErrorInvalidDeviceFunction;
+            regs = fa.numRegs;
+        }
+        if (regs != kRegsLaunch) return cudaErrorInvalidConfiguration;
+    }
     e = cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::SMEM);
     if (e != cudaSuccess) return e;
     BwdParams prm;
-    prm.lse = lse;
-    prm.delta = delta;
-    prm.dq_acc = dq_acc;
+    prm.lse2 = w.lse2;
+    prm.delta = w.delta;
+    prm.S_pad = w.S_pad;
     prm.dk = (__nv_bfloat16*)dk;
     prm.dv = (__nv_bfloat16*)dv;
     prm.sb = d.sb;
@@ -547,15 +691,15 @@ cudaError_t launch(cudaStream_t st, int sm_count, DeviceStatus* status, const At
     prm.causal = causal;
     prm.status = status;
     dim3 grid((d.S + BK - 1) / BK, d.H, d.B);
-    attn_bwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, tdo, prm);
+    attn_bwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, tdo, tdq, prm);
     note_launch();
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
 
-    const int64_t n8 = rows * (D / 8);
+    const int64_t n8 = (int64_t)d.B * d.H * d.S * (D / 8);
     int64_t blocks = (n8 + 255) / 256;
     if (blocks > (int64_t)sm_count * 32) blocks = (int64_t)sm_count * 32;
-    bwd_post_kernel<D><<<(unsigned)blocks, 256, 0, st>>>(dq_acc, (__nv_bfloat16*)dq, d, scale);
+    bwd_post_kernel<D><<<(unsigned)blocks, 256, 0, st>>>(w.dq_acc, (__nv_bfloat16*)dq, d, scale);
     note_launch();
     return cudaGetLastError();
 }
@@ -567,8 +711,9 @@ bool sm100_bwd_supported(hx_dtype dt, const AttnDims& d) {
 }
 
 uint64_t sm100_bwd_workspace_bytes(const AttnDims& d) {
-    const uint64_t rows = (uint64_t)d.B * d.H * d.S;
-    return align256(rows * 4) + align256(rows * (uint64_t)d.D * 4);
+    const uint64_t S_pad = (uint64_t)(d.S + 127) / 128 * 128;
+    const uint64_t tab = align256((uint64_t)d.B * d.H * S_pad * 4);
+    return 2 * tab + align256((uint64_t)d.B * d.H * d.S * (uint64_t)d.D * 4);
 }
 
 cudaError_t sm100_attn_bwd(cudaStream_t st, int sm_count, DeviceStatus* status,

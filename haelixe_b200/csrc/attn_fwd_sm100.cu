@@ -397,6 +397,17 @@ cudaError_t launch(cudaStream_t st, DeviceStatus* status, const AttnDims& d, con
         !make_tmap_bhsd(&tk, k, d.B, d.H, d.S, D, d.sb, d.sh, d.ss, 64, BN) ||
         !make_tmap_bhsd(&tv, v, d.B, d.H, d.S, D, d.sb, d.sh, d.ss, 64, BN))
         return cudaErrorInvalidValue;
+    // setmaxnreg.inc waits until the warp's share fits the block's launch
+    // allocation: launch only with exactly the register count the split assumes.
+    {
+        static int regs = -1;
+        if (regs < 0) {
+            cudaFuncAttributes fa;
+            if (cudaFuncGetAttributes(&fa, attn_fwd_kernel<D>) != cudaSuccess) return cudaErrorInvalidDeviceFunction;
+            regs = fa.numRegs;
+        }
+        if (regs != kRegsLaunch) return cudaErrorInvalidConfiguration;
+    }
     cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<D>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;

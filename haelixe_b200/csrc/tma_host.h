@@ -48,6 +48,22 @@ inline bool make_tmap_bhsd(CUtensorMap* map, const void* base, int B, int H, int
     return r == CUDA_SUCCESS;
 }
 
+// f32 tensor [n2][n1][n0] (n0 contiguous), box (b0, b1, 1), optional 128B swizzle.
+inline bool make_tmap_f32_3d(CUtensorMap* map, const void* base, uint64_t n0, uint64_t n1,
+                             uint64_t n2, int b0, int b1, bool swizzle128) {
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (fn == nullptr) return false;
+    cuuint64_t dims[3] = {n0, n1, n2};
+    cuuint64_t strides[2] = {n0 * 4, n0 * n1 * 4};
+    cuuint32_t box[3] = {(cuuint32_t)b0, (cuuint32_t)b1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 // Plain row-major bf16 matrix [rows][cols], box (box_cols, box_rows), 128B swizzle.
 inline bool make_tmap_2d(CUtensorMap* map, const void* base, int rows, int cols, int box_cols,
                          int box_rows) {
