@@ -22,11 +22,11 @@
 // The scale on dQ and dK is the factor the reference's backward omits
 // (flash_attention.rs:31,34-36).
 //
-// Warp roles of `main` (384 threads): warp 0 TMA producer (its lanes also
-// stage lse/delta of each query tile in smem), warp 1 MMA issuer (one
-// thread), warp 2 TMEM allocator, warps 4-7 the P/dS warpgroup (thread =
-// key row = TMEM lane), warps 8-11 the dQ drain warpgroup. All mbarrier
-// waits are bounded (sm100_ptx.cuh).
+// Warp roles of `main` (512 threads): warp 0 TMA producer (Q, dO tiles and
+// the lse/delta rows of each query tile), warp 1 MMA issuer (one thread),
+// warp 2 TMEM allocator, warps 4-7 and 8-11 two P/dS warpgroups that split
+// each query tile's columns (thread = key row = TMEM lane), warps 12-15 the
+// dQ drain warpgroup. All mbarrier waits are bounded (sm100_ptx.cuh).
 #include <math.h>
 
 #include "sm100_ptx.cuh"
@@ -38,15 +38,11 @@ namespace {
 using namespace ptx;
 
 constexpr int BK = 128;  // keys per CTA (UMMA M of S^T, dP^T, dV, dK)
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;
 // Register split (setmaxnreg) per SM sub-partition, one warp of each group:
-// control 56 + P/dS 256 + dQ drain 192 = 504 = 3 x 168 (the launch count,
-// checked on the host before every launch).
-constexpr int kRegsLaunch = 168;
-constexpr int kRegsCtl = 56;
-constexpr int kRegsCompute = 256;
-constexpr int kRegsDrain = 192;
-static_assert(kRegsCtl + kRegsCompute + kRegsDrain == 3 * kRegsLaunch, "register split");
+// control + 2 x P/dS + dQ drain = 512 = 4 x 128 (the launch count, checked on
+// the host before every launch); the shares depend on head_dim (BCfg).
+constexpr int kRegsLaunch = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
@@ -54,6 +50,10 @@ struct BCfg {
     static constexpr int BQ = D == 128 ? 64 : 128;  // queries per inner tile
     static constexpr bool DQ_T = D == 128;           // dQ computed transposed (M = D)
     static constexpr int QST = 3;                    // Q/dO/lse/delta ring depth
+    static constexpr int REGS_CTL = D == 128 ? 104 : 64;
+    static constexpr int REGS_COMPUTE = D == 128 ? 160 : 168;
+    static constexpr int REGS_DRAIN = D == 128 ? 88 : 112;
+    static_assert(REGS_CTL + 2 * REGS_COMPUTE + REGS_DRAIN == 4 * kRegsLaunch, "register split");
     static_assert(QST <= 4, "BBars holds 4 ring stages");
     static constexpr int CHUNK_K = BK * 128;         // bytes of a 64-column chunk of a K/V tile
     static constexpr int CHUNK_Q = BQ * 128;         // ... of a Q/dO tile
@@ -144,8 +144,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(bar_addr(bars->s_full[0]), 1);
         mbar_init(bar_addr(bars->s_full[1]), 1);
         mbar_init(bar_addr(bars->dp_full), 1);
-        mbar_init(bar_addr(bars->p_full), 128);
-        mbar_init(bar_addr(bars->ds_full), 128);
+        mbar_init(bar_addr(bars->p_full), 256);
+        mbar_init(bar_addr(bars->ds_full), 256);
         for (int s = 0; s < 2; ++s) {
             mbar_init(bar_addr(bars->dq_full[s]), 1);
             mbar_init(bar_addr(bars->dq_empty[s]), 128);
@@ -173,11 +173,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
     if (warp < 4) {
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegsCtl));
-    } else if (warp < 8) {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsCompute));
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(C::REGS_CTL));
+    } else if (warp < 12) {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(C::REGS_COMPUTE));
     } else {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsDrain));
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(C::REGS_DRAIN));
     }
 
     if (warp == 0) {
@@ -226,94 +226,159 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t idAcc = idesc_bf16_f32(BK, D, false, true);
             constexpr uint32_t idDQ =
                 C::DQ_T ? idesc_bf16_f32(D, BQ, true, true) : idesc_bf16_f32(BQ, D, true, true);
+            // Descriptor bases, built once: a K-step only adds its byte offset >> 4
+            // to the start-address field (every operand lies inside this CTA's smem).
             const uint32_t sK = smem_addr(sm + C::K_OFF), sV = smem_addr(sm + C::V_OFF),
                            sQ = smem_addr(sm + C::Q_OFF), sDO = smem_addr(sm + C::DO_OFF),
                            sDS = smem_addr(sm + C::DS_OFF);
-            // S^T or dP^T: A = K or V tile (K-major over D), B = Q or dO tile (K-major).
-            auto issue_sp = [&](uint32_t col, uint32_t a, uint32_t bq) {
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    umma_ss(tmem + col,
-                            sdesc_sw128(a + (kk / 4) * C::CHUNK_K + (kk % 4) * 32, 16, 1024),
-                            sdesc_sw128(bq + (kk / 4) * C::CHUNK_Q + (kk % 4) * 32, 16, 1024), idSP,
-                            kk > 0);
-            };
-            // dV or dK += (P^T or dS^T from TMEM) x (dO or Q tile, MN-major over D).
-            auto issue_acc = [&](uint32_t col, uint32_t a_col, uint32_t bq, bool first) {
-#pragma unroll
-                for (int kk = 0; kk < BQ / 16; ++kk)
-                    umma_ts(tmem + col, tmem + a_col + kk * 8,
-                            sdesc_sw128(bq + kk * 2048, C::CHUNK_Q, 1024), idAcc,
-                            (first && kk == 0) ? 0u : 1u);
-            };
-            auto issue_dq = [&](uint32_t col) {
-#pragma unroll
-                for (int kk = 0; kk < BK / 16; ++kk) {
-                    if (C::DQ_T)  // dQ^T = K^T dS^T: A = K^T (MN-major), B = dS^T (MN-major)
-                        umma_ss(tmem + col, sdesc_sw128(sK + kk * 2048, C::CHUNK_K, 1024),
-                                sdesc_sw128(sDS + kk * 2048, C::CHUNK_DS, 1024), idDQ, kk > 0);
-                    else  // dQ = dS K: A = dS (MN-major), B = K (MN-major)
-                        umma_ss(tmem + col, sdesc_sw128(sDS + kk * 2048, C::CHUNK_DS, 1024),
-                                sdesc_sw128(sK + kk * 2048, C::CHUNK_K, 1024), idDQ, kk > 0);
-                }
-            };
+            const uint64_t dKk = sdesc_sw128(sK, 16, 1024);               // K, K-major (A of S^T)
+            const uint64_t dVk = sdesc_sw128(sV, 16, 1024);               // V, K-major (A of dP^T)
+            const uint64_t dKm = sdesc_sw128(sK, C::CHUNK_K, 1024);      // K, MN-major (dQ)
+            const uint64_t dDSm = sdesc_sw128(sDS, C::CHUNK_DS, 1024);   // dS, MN-major (dQ)
+            const uint64_t dQk0 = sdesc_sw128(sQ, 16, 1024);              // Q stage 0, K-major
+            const uint64_t dDOk0 = sdesc_sw128(sDO, 16, 1024);            // dO stage 0, K-major
+            const uint64_t dQm0 = sdesc_sw128(sQ, C::CHUNK_Q, 1024);      // Q stage 0, MN-major
+            const uint64_t dDOm0 = sdesc_sw128(sDO, C::CHUNK_Q, 1024);    // dO stage 0, MN-major
+            constexpr uint64_t kStage = (uint64_t)(C::QT >> 4);           // per-stage offset
+            constexpr int KH = BQ / 32;  // K-steps of dV/dK per warpgroup half (see acc_a)
+            constexpr int NS = D / 16;   // K-steps of S^T / dP^T
+            constexpr int NA = BQ / 16;  // K-steps of dV / dK
+            constexpr int NQ = BK / 16;  // K-steps of dQ
+            // K-step offsets (in 16-byte units) of K-major and MN-major operands.
+            auto kmaj = [](int kk, int chunk) { return (uint64_t)(((kk / 4) * chunk + (kk % 4) * 32) >> 4); };
+            auto mnmaj = [](int kk) { return (uint64_t)((kk * 2048) >> 4); };
+            // A column of dV/dK K-step kk: warpgroup g packed its BQ/2 columns at the
+            // start of its own f32 columns [g*BQ/2, ...).
+            auto acc_a = [](int kk) { return (uint32_t)((kk / KH) * (BQ / 2) + (kk % KH) * 8); };
             auto s_col = [&](int it) { return C::C_S0 + (uint32_t)((it % C::NSB) * BQ); };
             auto q_wait = [&](int it) {
                 return mbar_wait(bar_addr(bars->q_full[it % C::QST]), (it / C::QST) & 1, abort_flag,
                                  p.status, 51);
             };
-            auto issue_s = [&](int it) {
-                issue_sp(s_col(it), sK, sQ + (it % C::QST) * C::QT);
-                umma_commit(bar_addr(bars->s_full[it % C::NSB]));
+            // One K-step of each GEMM.
+            auto s_step = [&](uint32_t col, uint64_t dq, int kk) {  // S^T += K Q^T
+                umma_ss(tmem + col, dKk + kmaj(kk, C::CHUNK_K), dq + kmaj(kk, C::CHUNK_Q), idSP, kk > 0);
+            };
+            auto dp_step = [&](uint64_t ddo, int kk) {  // dP^T += V dO^T
+                umma_ss(tmem + C::C_DP, dVk + kmaj(kk, C::CHUNK_K), ddo + kmaj(kk, C::CHUNK_Q), idSP,
+                        kk > 0);
+            };
+            auto acc_step = [&](uint32_t col, uint32_t a_col, uint64_t dbm, int kk, bool first) {
+                umma_ts(tmem + col, tmem + a_col + acc_a(kk), dbm + mnmaj(kk), idAcc,
+                        (first && kk == 0) ? 0u : 1u);
+            };
+            auto dq_step = [&](uint32_t col, int kk) {
+                if (C::DQ_T)  // dQ^T = K^T dS^T
+                    umma_ss(tmem + col, dKm + mnmaj(kk), dDSm + mnmaj(kk), idDQ, kk > 0);
+                else  // dQ = dS K
+                    umma_ss(tmem + col, dDSm + mnmaj(kk), dKm + mnmaj(kk), idDQ, kk > 0);
             };
             bool ok = mbar_wait(bar_addr(bars->kv_full), 0, abort_flag, p.status, 50) && q_wait(0);
-            if (ok) {
-                tc_fence_after();
-                issue_s(0);
-                if (C::NSB == 2 && n_it > 1) {
-                    ok = q_wait(1);
-                    if (ok) {
-                        tc_fence_after();
-                        issue_s(1);
-                    }
-                }
+            if constexpr (C::NSB == 2) {
+                // Per query tile i (consecutive MMAs alternate between independent GEMMs):
+                //   [P(i) ready]  dV(i) || S^T(i+1)          (different S^T buffers)
+                //   [dS(i) ready] dK(i) || dQ(i), then dQ(i) || dP^T(i+1)
+                // dP^T(i+1) overwrites dS^T(i): it starts after every dK(i) step.
                 if (ok) {
-                    issue_sp(C::C_DP, sV, sDO);
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < NS; ++kk) {
+                        s_step(C::C_S0, dQk0, kk);
+                        dp_step(dDOk0, kk);
+                    }
+                    umma_commit(bar_addr(bars->s_full[0]));
                     umma_commit(bar_addr(bars->dp_full));
                 }
-            }
-            for (int it = 0; ok && it < n_it; ++it) {
-                const int st = it % C::QST;
-                if (!(ok = mbar_wait(bar_addr(bars->p_full), it & 1, abort_flag, p.status, 52))) break;
-                tc_fence_after();
-                issue_acc(C::C_DV, s_col(it), sDO + st * C::QT, it == 0);
-                if (C::NSB == 1 && it + 1 < n_it) {
-                    // The single S^T buffer is free once dV(it) (issued above) has read P^T(it).
-                    if (!(ok = q_wait(it + 1))) break;
+                for (int it = 0; ok && it < n_it; ++it) {
+                    const int st = it % C::QST, stn = (it + 1) % C::QST;
+                    const bool next = it + 1 < n_it;
+                    const uint64_t dQm = dQm0 + st * kStage, dDOm = dDOm0 + st * kStage;
+                    const uint64_t dQkn = dQk0 + stn * kStage, dDOkn = dDOk0 + stn * kStage;
+                    const uint32_t cS = s_col(it), cSn = s_col(it + 1);
+                    const bool first = it == 0;
+                    if (!(ok = mbar_wait(bar_addr(bars->p_full), it & 1, abort_flag, p.status, 52))) break;
+                    if (next && !(ok = q_wait(it + 1))) break;
                     tc_fence_after();
-                    issue_s(it + 1);
+                    if (next) {
+#pragma unroll
+                        for (int kk = 0; kk < NS; ++kk) {
+                            if (kk < NA) acc_step(C::C_DV, cS, dDOm, kk, first);
+                            s_step(cSn, dQkn, kk);
+                        }
+                        umma_commit(bar_addr(bars->s_full[(it + 1) % 2]));
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < NA; ++kk) acc_step(C::C_DV, cS, dDOm, kk, first);
+                    }
+                    if (!(ok = mbar_wait(bar_addr(bars->ds_full), it & 1, abort_flag, p.status, 54))) break;
+                    if (!(ok = mbar_wait(bar_addr(bars->dq_empty[0]), (it & 1) ^ 1, abort_flag,
+                                         p.status, 55)))
+                        break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < NA; ++kk) {
+                        acc_step(C::C_DK, C::C_DP, dQm, kk, first);
+                        dq_step(C::C_DQ0, kk);
+                    }
+                    if (next) {
+#pragma unroll
+                        for (int kk = 0; kk < NS; ++kk) {
+                            dp_step(dDOkn, kk);
+                            if (NA + kk < NQ) dq_step(C::C_DQ0, NA + kk);
+                        }
+                    } else {
+#pragma unroll
+                        for (int kk = NA; kk < NQ; ++kk) dq_step(C::C_DQ0, kk);
+                    }
+                    umma_commit(bar_addr(bars->dq_full[0]));
+                    umma_commit(bar_addr(bars->q_empty[st]));
+                    if (next) umma_commit(bar_addr(bars->dp_full));
                 }
-                if (!(ok = mbar_wait(bar_addr(bars->ds_full), it & 1, abort_flag, p.status, 54))) break;
-                tc_fence_after();
-                issue_acc(C::C_DK, C::C_DP, sQ + st * C::QT, it == 0);
-                const int dqb = it % C::NDQ;
-                if (!(ok = mbar_wait(bar_addr(bars->dq_empty[dqb]), ((it / C::NDQ) & 1) ^ 1,
-                                     abort_flag, p.status, 55)))
-                    break;
-                tc_fence_after();
-                issue_dq(C::C_DQ0 + (uint32_t)(dqb * C::DQ_COLS));
-                umma_commit(bar_addr(bars->dq_full[dqb]));
-                umma_commit(bar_addr(bars->q_empty[st]));
-                if (it + 1 < n_it) {
-                    // dO(it+1) landed with Q(it+1), waited for when S^T(it+1) was issued.
-                    issue_sp(C::C_DP, sV, sDO + ((it + 1) % C::QST) * C::QT);
+            } else {
+                // One S^T buffer: S^T(i+1) waits for dV(i) to read P^T(i).
+                if (ok) {
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < NS; ++kk) s_step(C::C_S0, dQk0, kk);
+                    umma_commit(bar_addr(bars->s_full[0]));
+#pragma unroll
+                    for (int kk = 0; kk < NS; ++kk) dp_step(dDOk0, kk);
                     umma_commit(bar_addr(bars->dp_full));
                 }
-                if (C::NSB == 2 && it + 2 < n_it) {
-                    // S^T buffer of tile it is free: dV(it) read its P^T, in issue order.
-                    if (!(ok = q_wait(it + 2))) break;
+                for (int it = 0; ok && it < n_it; ++it) {
+                    const int st = it % C::QST, stn = (it + 1) % C::QST;
+                    const bool first = it == 0;
+                    const uint64_t dQm = dQm0 + st * kStage, dDOm = dDOm0 + st * kStage;
+                    if (!(ok = mbar_wait(bar_addr(bars->p_full), it & 1, abort_flag, p.status, 52))) break;
                     tc_fence_after();
-                    issue_s(it + 2);
+#pragma unroll
+                    for (int kk = 0; kk < NA; ++kk) acc_step(C::C_DV, C::C_S0, dDOm, kk, first);
+                    if (it + 1 < n_it) {
+                        if (!(ok = q_wait(it + 1))) break;
+                        tc_fence_after();
+#pragma unroll
+                        for (int kk = 0; kk < NS; ++kk) s_step(C::C_S0, dQk0 + stn * kStage, kk);
+                        umma_commit(bar_addr(bars->s_full[0]));
+                    }
+                    if (!(ok = mbar_wait(bar_addr(bars->ds_full), it & 1, abort_flag, p.status, 54))) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < NA; ++kk) acc_step(C::C_DK, C::C_DP, dQm, kk, first);
+                    const int dqb = it % C::NDQ;
+                    if (!(ok = mbar_wait(bar_addr(bars->dq_empty[dqb]), ((it / C::NDQ) & 1) ^ 1,
+                                         abort_flag, p.status, 55)))
+                        break;
+                    tc_fence_after();
+                    const uint32_t cq = C::C_DQ0 + (uint32_t)(dqb * C::DQ_COLS);
+#pragma unroll
+                    for (int kk = 0; kk < NQ; ++kk) dq_step(cq, kk);
+                    umma_commit(bar_addr(bars->dq_full[dqb]));
+                    umma_commit(bar_addr(bars->q_empty[st]));
+                    if (it + 1 < n_it) {
+#pragma unroll
+                        for (int kk = 0; kk < NS; ++kk) dp_step(dDOk0 + stn * kStage, kk);
+                        umma_commit(bar_addr(bars->dp_full));
+                    }
                 }
             }
             umma_commit(bar_addr(bars->acc_done));
@@ -327,144 +392,127 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             tmem_dealloc(tmem, 512);
         }
-    } else if (warp < 8) {
-        // ------------------------------------------------------------ P / dS warpgroup
+    } else if (warp < 12) {
+        // ------------------------------------------------------------ P / dS warpgroups
+        // Warpgroup g (warps 4-7: g=0, 8-11: g=1) owns columns [g*HC, (g+1)*HC) of
+        // every query tile; thread = key row = TMEM lane.
+        constexpr int HC = BQ / 2;  // columns per warpgroup
+        const int g = (warp - 4) / 4;
         const int wi = warp % 4;
-        const int r = wi * 32 + lane;  // key row within the tile (TMEM lane)
+        const int r = wi * 32 + lane;
         const int kr = k0 + r;
         const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
         const float sl2 = p.scale * kLog2e;
         uint8_t* ds_row = sm + C::DS_OFF + r * 128;
+        const int c0 = g * HC;  // first column of this warpgroup
         bool ok = true;
-        // P and dS stay in registers between the two phases: f32 when BQ = 64,
-        // packed bf16 when BQ = 128 (register budget).
-        constexpr bool kKeepF32 = BQ == 64;
-        constexpr int CHK = 64;  // columns per TMEM load batch
         for (int it = 0; it < n_it; ++it) {
             const int st = it % C::QST;
             const uint32_t ph = (it / C::QST) & 1;
             const int q0 = (i_start + it) * BQ;
-            const uint32_t cS = C::C_S0 + (uint32_t)((it % C::NSB) * BQ);
+            const uint32_t cS = C::C_S0 + (uint32_t)((it % C::NSB) * BQ) + c0;
+            const uint32_t cD = C::C_DP + c0;
             if (!(ok = mbar_wait(bar_addr(bars->q_full[st]), ph, abort_flag, p.status, 60))) break;
             if (!(ok = mbar_wait(bar_addr(bars->s_full[it % C::NSB]), (it / C::NSB) & 1, abort_flag,
                                  p.status, 61)))
                 break;
             tc_fence_after();
-            const float* lse2 = s_lse + st * BQ;
-            const float* del = s_del + st * BQ;
+            const float* lse2 = s_lse + st * BQ + c0;
+            const float* del = s_del + st * BQ + c0;
+            // Valid columns [lo, hi) of this row: q < S, key < S, causal q >= key.
             const bool need_mask = (q0 + BQ > p.S) || (k0 + BK > p.S) || (p.causal && k0 + BK - 1 > q0);
-            // P^T = exp2(S^T * scale*log2e - lse*log2e). Each 64-column batch is loaded
-            // with one wait; its packed P lands on S columns [c/2, c/2+32), already read.
-            float pr[kKeepF32 ? BQ : 1];
-            uint32_t pkeep[kKeepF32 ? 1 : BQ / 2];
-#pragma unroll
-            for (int c = 0; c < BQ; c += CHK) {
-                uint32_t x[CHK];
-                tmem_ld32(tl + cS + c, x);
-                tmem_ld32(tl + cS + c + 32, x + 32);
-                tmem_ld_wait();
-                reg_fence<CHK>(x);
-                uint32_t pk[CHK / 2];
-#pragma unroll
-                for (int g = 0; g < CHK / 4; ++g) {
-                    const float4 l4 = reinterpret_cast<const float4*>(lse2 + c)[g];
-                    const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-#pragma unroll
-                    for (int e = 0; e < 4; e += 2) {
-                        const int i = 4 * g + e;
-                        float p0 = ex2(fmaf(__uint_as_float(x[i]), sl2, -lv[e]));
-                        float p1 = ex2(fmaf(__uint_as_float(x[i + 1]), sl2, -lv[e + 1]));
-                        if (need_mask) {
-                            const int qa = q0 + c + i, qb = qa + 1;
-                            p0 = (qa < p.S && kr < p.S && (!p.causal || kr <= qa)) ? p0 : 0.f;
-                            p1 = (qb < p.S && kr < p.S && (!p.causal || kr <= qb)) ? p1 : 0.f;
-                        }
-                        pk[i / 2] = pack_bf16(p0, p1);
-                        if constexpr (kKeepF32) {
-                            pr[c + i] = p0;
-                            pr[c + i + 1] = p1;
-                        } else {
-                            pkeep[(c + i) / 2] = pk[i / 2];
-                        }
-                    }
-                }
-                tmem_st32(tl + cS + c / 2, pk);
+            int lo = 0, hi = HC;
+            if (need_mask) {
+                hi = kr < p.S ? min(HC, p.S - q0 - c0) : 0;
+                if (p.causal) lo = max(0, kr - q0 - c0);
             }
+            // P^T = exp2(S^T * scale*log2e - lse*log2e) for HC columns, loaded with
+            // one wait; the packed result lands on the first HC/2 of these columns.
+            uint32_t x[HC];
+#pragma unroll
+            for (int c = 0; c < HC; c += 32) tmem_ld32(tl + cS + c, x + c);
+            tmem_ld_wait();
+            reg_fence<HC>(x);
+            float pr[HC];
+#pragma unroll
+            for (int q4 = 0; q4 < HC / 4; ++q4) {
+                const float4 l4 = reinterpret_cast<const float4*>(lse2)[q4];
+                pr[4 * q4 + 0] = ex2(fmaf(__uint_as_float(x[4 * q4 + 0]), sl2, -l4.x));
+                pr[4 * q4 + 1] = ex2(fmaf(__uint_as_float(x[4 * q4 + 1]), sl2, -l4.y));
+                pr[4 * q4 + 2] = ex2(fmaf(__uint_as_float(x[4 * q4 + 2]), sl2, -l4.z));
+                pr[4 * q4 + 3] = ex2(fmaf(__uint_as_float(x[4 * q4 + 3]), sl2, -l4.w));
+            }
+            if (need_mask) {
+#pragma unroll
+                for (int c = 0; c < HC; ++c) pr[c] = (c >= lo && c < hi) ? pr[c] : 0.f;
+            }
+            uint32_t pk[HC / 2];
+#pragma unroll
+            for (int i = 0; i < HC / 2; ++i) pk[i] = pack_bf16(pr[2 * i], pr[2 * i + 1]);
+#pragma unroll
+            for (int c = 0; c < HC / 2; c += 16) tmem_st16(tl + cS + c, pk + c);
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(bar_addr(bars->p_full));
 
             if (!(ok = mbar_wait(bar_addr(bars->dp_full), it & 1, abort_flag, p.status, 62))) break;
             tc_fence_after();
-            // dS^T = P^T (dP^T - delta) -> TMEM (over dP, same batch argument) and the
-            // 128-byte-swizzled smem tile read by the dQ MMA.
+            // dS^T = P^T (dP^T - delta) -> TMEM (over this warpgroup's dP columns) and
+            // the 128-byte-swizzled smem tile the dQ MMA reads.
 #pragma unroll
-            for (int c = 0; c < BQ; c += CHK) {
-                uint32_t x[CHK];
-                tmem_ld32(tl + C::C_DP + c, x);
-                tmem_ld32(tl + C::C_DP + c + 32, x + 32);
-                tmem_ld_wait();
-                reg_fence<CHK>(x);
-                uint32_t dk[CHK / 2];
+            for (int c = 0; c < HC; c += 32) tmem_ld32(tl + cD + c, x + c);
+            tmem_ld_wait();
+            reg_fence<HC>(x);
 #pragma unroll
-                for (int g = 0; g < CHK / 4; ++g) {
-                    const float4 d4 = reinterpret_cast<const float4*>(del + c)[g];
-                    const float dl[4] = {d4.x, d4.y, d4.z, d4.w};
+            for (int q4 = 0; q4 < HC / 4; ++q4) {
+                const float4 d4 = reinterpret_cast<const float4*>(del)[q4];
+                const float a0 = pr[4 * q4 + 0] * (__uint_as_float(x[4 * q4 + 0]) - d4.x);
+                const float a1 = pr[4 * q4 + 1] * (__uint_as_float(x[4 * q4 + 1]) - d4.y);
+                const float a2 = pr[4 * q4 + 2] * (__uint_as_float(x[4 * q4 + 2]) - d4.z);
+                const float a3 = pr[4 * q4 + 3] * (__uint_as_float(x[4 * q4 + 3]) - d4.w);
+                pk[2 * q4] = pack_bf16(a0, a1);
+                pk[2 * q4 + 1] = pack_bf16(a2, a3);
+            }
 #pragma unroll
-                    for (int e = 0; e < 4; e += 2) {
-                        const int i = 4 * g + e;
-                        float p0, p1;
-                        if constexpr (kKeepF32) {
-                            p0 = pr[c + i];
-                            p1 = pr[c + i + 1];
-                        } else {
-                            p0 = __uint_as_float(pkeep[(c + i) / 2] << 16);
-                            p1 = __uint_as_float(pkeep[(c + i) / 2] & 0xffff0000u);
-                        }
-                        const float d0 = p0 * (__uint_as_float(x[i]) - dl[e]);
-                        const float d1 = p1 * (__uint_as_float(x[i + 1]) - dl[e + 1]);
-                        dk[i / 2] = pack_bf16(d0, d1);
-                    }
-                }
-                tmem_st32(tl + C::C_DP + c / 2, dk);
-                uint8_t* chunk_row = ds_row + (c / 64) * C::CHUNK_DS;
+            for (int c = 0; c < HC / 2; c += 16) tmem_st16(tl + cD + c, pk + c);
+            // smem: 16-byte piece u of the 128-byte row of 64-column chunk k holds
+            // columns k*64 + 8u .. +7.
 #pragma unroll
-                for (int u = 0; u < 8; ++u)
-                    *reinterpret_cast<uint4*>(chunk_row + ((u ^ (r & 7)) * 16)) =
-                        make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+            for (int u8 = 0; u8 < HC / 8; ++u8) {
+                const int col = c0 + 8 * u8;
+                const int chunk = col / 64, u = (col % 64) / 8;
+                *reinterpret_cast<uint4*>(ds_row + chunk * C::CHUNK_DS + ((u ^ (r & 7)) * 16)) =
+                    make_uint4(pk[4 * u8], pk[4 * u8 + 1], pk[4 * u8 + 2], pk[4 * u8 + 3]);
             }
             tmem_st_wait();
             fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
             tc_fence_before();
             mbar_arrive(bar_addr(bars->ds_full));
         }
-        // dK, dV epilogue
+        // Epilogue: warpgroup 0 stores dV, warpgroup 1 stores dK (times scale).
         if (ok && mbar_wait(bar_addr(bars->acc_done), 0, abort_flag, p.status, 63)) {
             tc_fence_after();
             const bool store = kr < p.S;
             const int64_t off = (int64_t)b * p.sb + (int64_t)h * p.sh + (int64_t)kr * p.ss;
+            const uint32_t col = g ? C::C_DK : C::C_DV;
+            const float mul = g ? p.scale : 1.f;
+            __nv_bfloat16* dst = (g ? p.dk : p.dv) + off;
 #pragma unroll
-            for (int which = 0; which < 2; ++which) {
-                const uint32_t col = which ? C::C_DK : C::C_DV;
-                const float mul = which ? p.scale : 1.f;
-                __nv_bfloat16* dst = (which ? p.dk : p.dv) + off;
+            for (int c = 0; c < D; c += 32) {
+                uint32_t v[32];
+                tmem_ld32(tl + col + c, v);
+                tmem_ld_wait();
+                reg_fence<32>(v);
+                if (store) {
+                    uint4* d4 = reinterpret_cast<uint4*>(dst + c);
 #pragma unroll
-                for (int c = 0; c < D; c += 32) {
-                    uint32_t v[32];
-                    tmem_ld32(tl + col + c, v);
-                    tmem_ld_wait();
-                    reg_fence<32>(v);
-                    if (store) {
-                        uint4* d4 = reinterpret_cast<uint4*>(dst + c);
-#pragma unroll
-                        for (int q4 = 0; q4 < 4; ++q4) {
-                            uint4 o;
-                            o.x = pack_bf16(__uint_as_float(v[8 * q4 + 0]) * mul, __uint_as_float(v[8 * q4 + 1]) * mul);
-                            o.y = pack_bf16(__uint_as_float(v[8 * q4 + 2]) * mul, __uint_as_float(v[8 * q4 + 3]) * mul);
-                            o.z = pack_bf16(__uint_as_float(v[8 * q4 + 4]) * mul, __uint_as_float(v[8 * q4 + 5]) * mul);
-                            o.w = pack_bf16(__uint_as_float(v[8 * q4 + 6]) * mul, __uint_as_float(v[8 * q4 + 7]) * mul);
-                            d4[q4] = o;
-                        }
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        uint4 o;
+                        o.x = pack_bf16(__uint_as_float(v[8 * q4 + 0]) * mul, __uint_as_float(v[8 * q4 + 1]) * mul);
+                        o.y = pack_bf16(__uint_as_float(v[8 * q4 + 2]) * mul, __uint_as_float(v[8 * q4 + 3]) * mul);
+                        o.z = pack_bf16(__uint_as_float(v[8 * q4 + 4]) * mul, __uint_as_float(v[8 * q4 + 5]) * mul);
+                        o.w = pack_bf16(__uint_as_float(v[8 * q4 + 6]) * mul, __uint_as_float(v[8 * q4 + 7]) * mul);
+                        d4[q4] = o;
                     }
                 }
             }
@@ -479,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int wi = warp % 4;
         const int r = wi * 32 + lane;  // TMEM lane: d (dQ^T) or query row (dQ)
         const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
-        const bool elected = (warp == 8 && lane == 0);
+        const bool elected = (warp == 12 && lane == 0);
         float* stage = (float*)(sm + C::DQS_OFF);
         for (int it = 0; it < n_it; ++it) {
             const int buf = it % C::NDQ;

@@ -195,6 +195,20 @@ def test_misaligned_operands_take_a_correct_path():
     _check("O", o, ro, torch.bfloat16)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
+@pytest.mark.parametrize("layout", ["bshd", "bhsd"])
+def test_reassemble_heads_kernel(dtype, layout):
+    from haelixe_b200.sharding import reassemble_heads
+    n, B, Hs, S, D = 4, 2, 3, 37, 64
+    g = torch.randn(n, B, Hs, S, D, device="cuda").to(dtype)
+    out = torch.empty((B, S, n * Hs, D) if layout == "bshd" else (B, n * Hs, S, D),
+                      device="cuda", dtype=dtype)
+    reassemble_heads(g, out, n, layout)
+    full = g.permute(1, 0, 2, 3, 4).reshape(B, n * Hs, S, D)
+    ref = full.permute(0, 2, 1, 3) if layout == "bshd" else full
+    assert torch.equal(out, ref)
+
+
 def _sampled_full_size(B, H, S, D, causal, rope_base=None, samples=((0, 0),)):
     """Full-size run on the GPU; oracle on sampled (b, h) slices; identities on all."""
     torch.manual_seed(0)
