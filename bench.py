@@ -195,7 +195,7 @@ def run_reference(a):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded N(0,1), bf16-rounded)", "config": config_of(a, 1),
+        "data": "synthetic (seeded N(0,1), bf16-rounded)", "config": config_of(a, a.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": ora.num_threads(),
                          "kind": "port",
                          "sample": f"one (b,h) slice (S={S}, D={D}) per step: RoPE, fwd+bwd with "

@@ -97,7 +97,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     using C = Cfg<D>;
     using B = Bars<C::STAGES>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    // 1024-byte aligned base, derived from the shared array itself so that the
+    // compiler keeps every access through `sm` in the shared state space.
+    uint8_t* sm = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     B* bars = (B*)(sm + C::BAR_OFF);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
