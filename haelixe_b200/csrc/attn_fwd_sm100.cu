@@ -73,6 +73,7 @@ struct Bars {
     uint64_t q_full;
     uint64_t k_full[STAGES], k_empty[STAGES], v_full[STAGES], v_empty[STAGES];
     uint64_t s_full[NWG], p_full[NWG], o_full[NWG];
+    uint64_t turn[NWG];  // ping-pong token between the softmax warpgroups
     uint64_t done;
     uint32_t tmem_base;
     int abort_flag;
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(bar_addr(bars->s_full[w]), 1);
             mbar_init(bar_addr(bars->p_full[w]), BM);
             mbar_init(bar_addr(bars->o_full[w]), 1);
+            mbar_init(bar_addr(bars->turn[w]), BM);
         }
         mbar_init(bar_addr(bars->done), 1);
         fence_mbar_init();
@@ -203,25 +205,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (warp == 1 && lane == 0) {
             constexpr uint32_t idS = idesc_bf16_f32(BM, BN, false, false);
             constexpr uint32_t idO = idesc_bf16_f32(BM, D, false, true);
-            const uint32_t sQ = smem_addr(sm + C::Q_OFF), sK = smem_addr(sm + C::K_OFF),
-                           sV = smem_addr(sm + C::V_OFF);
+            // Descriptors are built once; a K step, a stage or a query tile
+            // only moves the start address field (bits 0-13, address >> 4).
+            // The high word of every descriptor here is the same (SBO 1024,
+            // version, 128-byte swizzle); the low word holds the start address
+            // >> 4 (and LBO), so a K step, a stage or a query tile is a 32-bit
+            // add to a base built once.
+            const uint32_t hi = (uint32_t)(sdesc_sw128(0, 16, 1024) >> 32);
+            const uint32_t lQ = (uint32_t)sdesc_sw128(smem_addr(sm + C::Q_OFF), 16, 1024);
+            const uint32_t lK = (uint32_t)sdesc_sw128(smem_addr(sm + C::K_OFF), 16, 1024);
+            const uint32_t lV = (uint32_t)sdesc_sw128(smem_addr(sm + C::V_OFF), C::CHUNK, 1024);
+            constexpr uint32_t kTile = C::TILE >> 4;
+            auto kmaj = [](int kk) { return (uint32_t)(((kk / 4) * C::CHUNK + (kk % 4) * 32) >> 4); };
             auto issue_S = [&](int w, int st) {
                 const uint32_t dS = tmem + (w ? C::S_COL1 : C::S_COL0);
+                const uint32_t dq = lQ + w * kTile, dk = lK + st * kTile;
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (kk / 4) * C::CHUNK + (kk % 4) * 32;
-                    umma_ss(dS, sdesc_sw128(sQ + w * C::TILE + off, 16, 1024),
-                            sdesc_sw128(sK + st * C::TILE + off, 16, 1024), idS, kk > 0);
-                }
+                for (int kk = 0; kk < D / 16; ++kk)
+                    umma_ss(dS, desc_of(dq + kmaj(kk), hi), desc_of(dk + kmaj(kk), hi), idS, kk > 0);
                 umma_commit(bar_addr(bars->s_full[w]));
             };
             auto issue_PV = [&](int w, int st, int j) {
                 const uint32_t dO = tmem + (w ? C::O_COL1 : C::O_COL0);
                 const uint32_t aP = tmem + (w ? C::S_COL1 : C::S_COL0);
+                const uint32_t dv = lV + st * kTile;
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk)
-                    umma_ts(dO, aP + kk * 8,
-                            sdesc_sw128(sV + st * C::TILE + kk * 2048, C::CHUNK, 1024), idO,
+                    umma_ts(dO, aP + kk * 8, desc_of(dv + kk * (2048 >> 4), hi), idO,
                             (j > 0 || kk > 0) ? 1u : 0u);
                 umma_commit(bar_addr(bars->o_full[w]));
             };
@@ -295,18 +305,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int kbase = j * BN;
             const bool need_mask =
                 (kbase + BN > p.S) || (p.causal && kbase + BN - 1 > m0 + w * BM);
-            float mx = -INFINITY;
             if (need_mask) {
                 const int lim = p.causal ? min(p.S - 1, row) : p.S - 1;
 #pragma unroll
-                for (int c = 0; c < BN; ++c) {
-                    const float x = (kbase + c <= lim) ? __uint_as_float(s[c]) : -INFINITY;
-                    s[c] = __float_as_uint(x);
-                    mx = fmaxf(mx, x);
-                }
-            } else {
+                for (int c = 0; c < BN; ++c)
+                    if (kbase + c > lim) s[c] = __float_as_uint(-INFINITY);
+            }
+            // Two independent three-input max chains.
+            float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < BN; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+            for (int c = 0; c < BN; c += 4) {
+                mx0 = max3(mx0, __uint_as_float(s[c]), __uint_as_float(s[c + 1]));
+                mx1 = max3(mx1, __uint_as_float(s[c + 2]), __uint_as_float(s[c + 3]));
+            }
+            const float mx = fmaxf(mx0, mx1);
+            // Ping-pong: the two warpgroups take turns on the exp2 section (the
+            // MUFU is shared), so one runs its exps while the tensor core works
+            // on the other's PV and next S. Warpgroup 0 goes first on tile j
+            // (after warpgroup 1 finished tile j-1), warpgroup 1 after warpgroup 0
+            // finished tile j; a warpgroup with no such partner tile does not wait.
+            {
+                const int other = n_w[w ^ 1];
+                const int jt = w == 0 ? j - 1 : j;  // partner tile that must be done
+                if (jt >= 0 && jt < other &&
+                    !(ok = mbar_wait(bar_addr(bars->turn[w]), jt & 1, abort_flag, p.status, 33)))
+                    break;
             }
             const float m_new = fmaxf(m_run, mx * p.sl2);
             float m_use = m_run, alpha = 1.f;
@@ -319,20 +342,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                 rescale = true;
             }
             l_run *= alpha;
-            const float neg = -m_use;
-            float sum = 0.f;
+            // x = s * scale * log2(e) - m and the row sum run two columns per
+            // instruction (f32x2); the exponentials stay on the MUFU.
+            const uint64_t sl2x2 = f2_pack(p.sl2, p.sl2);
+            const uint64_t negx2 = f2_pack(-m_use, -m_use);
+            uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = sum_a;
 #pragma unroll
             for (int c = 0; c < BN; c += 32) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float p0 = ex2(fmaf(__uint_as_float(s[c + 2 * i]), p.sl2, neg));
-                    const float p1 = ex2(fmaf(__uint_as_float(s[c + 2 * i + 1]), p.sl2, neg));
-                    sum += p0 + p1;
+                    const uint64_t x = f2_fma(
+                        f2_pack(__uint_as_float(s[c + 2 * i]), __uint_as_float(s[c + 2 * i + 1])),
+                        sl2x2, negx2);
+                    float x0, x1;
+                    f2_unpack(x, x0, x1);
+                    const float p0 = ex2(x0), p1 = ex2(x1);
+                    if (i & 1)
+                        sum_b = f2_add(sum_b, f2_pack(p0, p1));
+                    else
+                        sum_a = f2_add(sum_a, f2_pack(p0, p1));
                     pk[i] = pack_bf16(p0, p1);
                 }
                 tmem_st16(tS + c / 2, pk);
             }
+            float s0, s1;
+            f2_unpack(f2_add(sum_a, sum_b), s0, s1);
+            const float sum = s0 + s1;
+            mbar_arrive(bar_addr(bars->turn[w ^ 1]));  // the partner's turn
             // O is rescaled after P is written (the scores are dead by then)
             // and before P is published: PV(j) cannot start earlier, and
             // PV(j-1) of this tile must have landed.
