@@ -32,9 +32,22 @@ METRIC = "attn fwd+bwd TFLOP/s and % of BF16 tensor peak at 1/2/4/8 B200 vs host
 UNIT = "TFLOP/s"
 # Peak used for roofline.frac: the pool's measured cuBLAS bf16 figures.
 FALLBACK_PEAK_TFLOPS = 1590.0
-# DRAM bytes per launch of the dominant kernel from one ncu capture of the
-# same command (profiles/ summary named for the kernel); None until captured.
-DOMINANT_KERNEL_TRAFFIC_BYTES = None
+# DRAM bytes (read + write) per launch of the dominant kernel (the tcgen05
+# backward) at B4 H32 S8192 D128: an ncu capture of the same kernel at B1
+# (profiles/attn_bwd_kernel_B1_H32_S8192_D128.md: 404.9 MB read + 223.1 MB
+# written) scaled by 4, since the heads are independent and the traffic grows
+# with B*H. Valid for the default workload only; other shapes report None.
+DOMINANT_KERNEL_TRAFFIC_BYTES = 4 * (404.868352e6 + 223.088384e6)
+TRAFFIC_WORKLOAD = (4, 32, 8192, 128)
+
+
+def traffic_per_launch(dom, B, H, S, D):
+    """DRAM bytes per launch of the dominant kernel on this rank, scaled from
+    the captured workload by the number of (batch, head) slices it processes."""
+    b0, h0, s0, d0 = TRAFFIC_WORKLOAD
+    if dom != "bwd" or (S, D) != (s0, d0):
+        return None
+    return DOMINANT_KERNEL_TRAFFIC_BYTES * (B * H) / (b0 * h0)
 
 
 def parse():
@@ -345,7 +358,7 @@ def run_haelixe(a):
             "roofline": {"bound": "tensor", "kernel": f"attention {dom} ({ctx.last_path})",
                          "achieved": achieved, "peak": peak, "peak_source": peak_src,
                          "unit": "TFLOP/s", "frac": achieved / peak,
-                         "traffic": DOMINANT_KERNEL_TRAFFIC_BYTES},
+                         "traffic": traffic_per_launch(dom, B, Hl, S, D)},
             "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
             "fraction_of_peak": value / world / peak,
             "gpu_launches": int(launches),
