@@ -86,12 +86,15 @@ struct BBars {
     uint64_t kv_full;
     uint64_t q_full[4], q_empty[4];  // indexed by ring stage (QST <= 4)
     uint64_t s_full[2], dp_full, p_full, ds_full;
+    uint64_t sfree[2], dpfree;  // TMEM hand-offs from the accumulate to the recompute issuer
     uint64_t dq_full[2], dq_empty[2];
     uint64_t dqs_free, dqs_full;
-    uint64_t acc_done, done;
+    uint64_t acc_done, done, done_r;
     uint32_t tmem_base;
     int abort_flag;
 };
+
+static_assert(sizeof(BBars) <= 256, "barrier block");
 
 struct BwdParams {
     const float* lse2;   // [B*H][S_pad]: lse * log2(e), 0 past S
@@ -146,6 +149,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(bar_addr(bars->s_full[0]), 1);
         mbar_init(bar_addr(bars->s_full[1]), 1);
         mbar_init(bar_addr(bars->dp_full), 1);
+        mbar_init(bar_addr(bars->sfree[0]), 1);
+        mbar_init(bar_addr(bars->sfree[1]), 1);
+        mbar_init(bar_addr(bars->dpfree), 1);
         mbar_init(bar_addr(bars->p_full), 256);
         mbar_init(bar_addr(bars->ds_full), 256);
         for (int s = 0; s < 2; ++s) {
@@ -156,6 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(bar_addr(bars->dqs_full), 128);
         mbar_init(bar_addr(bars->acc_done), 1);
         mbar_init(bar_addr(bars->done), 1);
+        mbar_init(bar_addr(bars->done_r), 1);
         fence_mbar_init();
         fence_proxy_async();
     }
@@ -222,166 +229,113 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncthreads();
     } else if (warp < 4) {
-        // ------------------------------------------------------------ MMA issuer (warp 1, lane 0)
-        if (warp == 1 && lane == 0) {
-            constexpr uint32_t idSP = idesc_bf16_f32(BK, BQ, false, false);
-            constexpr uint32_t idAcc = idesc_bf16_f32(BK, D, false, true);
-            constexpr uint32_t idDQ =
-                C::DQ_T ? idesc_bf16_f32(D, BQ, true, true) : idesc_bf16_f32(BQ, D, true, true);
-            // Descriptor bases, built once: a K-step only adds its byte offset >> 4
-            // to the start-address field (every operand lies inside this CTA's smem).
-            const uint32_t sK = smem_addr(sm + C::K_OFF), sV = smem_addr(sm + C::V_OFF),
-                           sQ = smem_addr(sm + C::Q_OFF), sDO = smem_addr(sm + C::DO_OFF),
-                           sDS = smem_addr(sm + C::DS_OFF);
-            const uint64_t dKk = sdesc_sw128(sK, 16, 1024);               // K, K-major (A of S^T)
-            const uint64_t dVk = sdesc_sw128(sV, 16, 1024);               // V, K-major (A of dP^T)
-            const uint64_t dKm = sdesc_sw128(sK, C::CHUNK_K, 1024);      // K, MN-major (dQ)
-            const uint64_t dDSm = sdesc_sw128(sDS, C::CHUNK_DS, 1024);   // dS, MN-major (dQ)
-            const uint64_t dQk0 = sdesc_sw128(sQ, 16, 1024);              // Q stage 0, K-major
-            const uint64_t dDOk0 = sdesc_sw128(sDO, 16, 1024);            // dO stage 0, K-major
-            const uint64_t dQm0 = sdesc_sw128(sQ, C::CHUNK_Q, 1024);      // Q stage 0, MN-major
-            const uint64_t dDOm0 = sdesc_sw128(sDO, C::CHUNK_Q, 1024);    // dO stage 0, MN-major
-            constexpr uint64_t kStage = (uint64_t)(C::QT >> 4);           // per-stage offset
-            constexpr int KH = BQ / 32;  // K-steps of dV/dK per warpgroup half (see acc_a)
-            constexpr int NS = D / 16;   // K-steps of S^T / dP^T
-            constexpr int NA = BQ / 16;  // K-steps of dV / dK
-            constexpr int NQ = BK / 16;  // K-steps of dQ
-            // K-step offsets (in 16-byte units) of K-major and MN-major operands.
-            auto kmaj = [](int kk, int chunk) { return (uint64_t)(((kk / 4) * chunk + (kk % 4) * 32) >> 4); };
-            auto mnmaj = [](int kk) { return (uint64_t)((kk * 2048) >> 4); };
+        // ------------------------------------------------------------ MMA issuers
+        // Two threads issue MMAs, each waiting only on its own inputs, so one
+        // keeps the tensor core fed while the other waits (a single issuing
+        // thread leaves the pipe idle during every mbarrier wait):
+        //   warp 3 lane 0 (recompute): S^T(i) = K Q^T and dP^T(i) = V dO^T;
+        //   warp 1 lane 0 (accumulate): dV += P^T dO, dK += dS^T Q, dQ(i).
+        // TMEM hand-offs between the two go through mbarriers committed by the
+        // thread whose MMAs free a buffer: sfree[b] after dV reads P^T from S
+        // buffer b, dpfree after dK reads dS^T from the dP^T columns.
+        constexpr uint32_t idSP = idesc_bf16_f32(BK, BQ, false, false);
+        constexpr uint32_t idAcc = idesc_bf16_f32(BK, D, false, true);
+        constexpr uint32_t idDQ =
+            C::DQ_T ? idesc_bf16_f32(D, BQ, true, true) : idesc_bf16_f32(BQ, D, true, true);
+        constexpr uint64_t kStage = (uint64_t)(C::QT >> 4);  // per-stage descriptor offset
+        constexpr int KH = BQ / 32;  // K-steps of dV/dK per warpgroup half (see acc_a)
+        constexpr int NS = D / 16;   // K-steps of S^T / dP^T
+        constexpr int NA = BQ / 16;  // K-steps of dV / dK
+        constexpr int NQ = BK / 16;  // K-steps of dQ
+        // K-step offsets (in 16-byte units) of K-major and MN-major operands.
+        auto kmaj = [](int kk, int chunk) { return (uint64_t)(((kk / 4) * chunk + (kk % 4) * 32) >> 4); };
+        auto mnmaj = [](int kk) { return (uint64_t)((kk * 2048) >> 4); };
+        // Descriptor bases, built once: a K-step only adds its byte offset >> 4
+        // to the start-address field (every operand lies inside this CTA's smem).
+        const uint32_t sK = smem_addr(sm + C::K_OFF), sV = smem_addr(sm + C::V_OFF),
+                       sQ = smem_addr(sm + C::Q_OFF), sDO = smem_addr(sm + C::DO_OFF),
+                       sDS = smem_addr(sm + C::DS_OFF);
+        bool ok = true;
+        if (warp == 3 && lane == 0) {
+            // -------- recompute issuer
+            const uint64_t dKk = sdesc_sw128(sK, 16, 1024);     // K, K-major (A of S^T)
+            const uint64_t dVk = sdesc_sw128(sV, 16, 1024);     // V, K-major (A of dP^T)
+            const uint64_t dQk0 = sdesc_sw128(sQ, 16, 1024);    // Q stage 0, K-major
+            const uint64_t dDOk0 = sdesc_sw128(sDO, 16, 1024);  // dO stage 0, K-major
+            ok = mbar_wait(bar_addr(bars->kv_full), 0, abort_flag, p.status, 50);
+            for (int it = 0; ok && it < n_it; ++it) {
+                const int st = it % C::QST, b = it % C::NSB;
+                if (!(ok = mbar_wait(bar_addr(bars->q_full[st]), (it / C::QST) & 1, abort_flag,
+                                     p.status, 51)))
+                    break;
+                // S^T buffer b is free once dV(it - NSB) has read P^T from it.
+                if (!(ok = mbar_wait(bar_addr(bars->sfree[b]), ((it / C::NSB) & 1) ^ 1, abort_flag,
+                                     p.status, 56)))
+                    break;
+                tc_fence_after();
+                const uint32_t cS = C::C_S0 + (uint32_t)(b * BQ);
+                const uint64_t dq = dQk0 + st * kStage, ddo = dDOk0 + st * kStage;
+#pragma unroll
+                for (int kk = 0; kk < NS; ++kk)
+                    umma_ss(tmem + cS, dKk + kmaj(kk, C::CHUNK_K), dq + kmaj(kk, C::CHUNK_Q), idSP, kk > 0);
+                umma_commit(bar_addr(bars->s_full[b]));
+                // The dP^T columns are free once dK(it - 1) has read dS^T(it - 1).
+                if (!(ok = mbar_wait(bar_addr(bars->dpfree), (it & 1) ^ 1, abort_flag, p.status, 57)))
+                    break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < NS; ++kk)
+                    umma_ss(tmem + C::C_DP, dVk + kmaj(kk, C::CHUNK_K), ddo + kmaj(kk, C::CHUNK_Q), idSP,
+                            kk > 0);
+                umma_commit(bar_addr(bars->dp_full));
+            }
+            umma_commit(bar_addr(bars->done_r));
+            mbar_wait_drain(bar_addr(bars->done_r), 0);
+        } else if (warp == 1 && lane == 0) {
+            // -------- accumulate issuer
+            const uint64_t dKm = sdesc_sw128(sK, C::CHUNK_K, 1024);     // K, MN-major (dQ)
+            const uint64_t dDSm = sdesc_sw128(sDS, C::CHUNK_DS, 1024);  // dS, MN-major (dQ)
+            const uint64_t dQm0 = sdesc_sw128(sQ, C::CHUNK_Q, 1024);    // Q stage 0, MN-major
+            const uint64_t dDOm0 = sdesc_sw128(sDO, C::CHUNK_Q, 1024);  // dO stage 0, MN-major
             // A column of dV/dK K-step kk: warpgroup g packed its BQ/2 columns at the
             // start of its own f32 columns [g*BQ/2, ...).
             auto acc_a = [](int kk) { return (uint32_t)((kk / KH) * (BQ / 2) + (kk % KH) * 8); };
-            auto s_col = [&](int it) { return C::C_S0 + (uint32_t)((it % C::NSB) * BQ); };
-            auto q_wait = [&](int it) {
-                return mbar_wait(bar_addr(bars->q_full[it % C::QST]), (it / C::QST) & 1, abort_flag,
-                                 p.status, 51);
-            };
-            // One K-step of each GEMM.
-            auto s_step = [&](uint32_t col, uint64_t dq, int kk) {  // S^T += K Q^T
-                umma_ss(tmem + col, dKk + kmaj(kk, C::CHUNK_K), dq + kmaj(kk, C::CHUNK_Q), idSP, kk > 0);
-            };
-            auto dp_step = [&](uint64_t ddo, int kk) {  // dP^T += V dO^T
-                umma_ss(tmem + C::C_DP, dVk + kmaj(kk, C::CHUNK_K), ddo + kmaj(kk, C::CHUNK_Q), idSP,
-                        kk > 0);
-            };
-            auto acc_step = [&](uint32_t col, uint32_t a_col, uint64_t dbm, int kk, bool first) {
-                umma_ts(tmem + col, tmem + a_col + acc_a(kk), dbm + mnmaj(kk), idAcc,
-                        (first && kk == 0) ? 0u : 1u);
-            };
-            auto dq_step = [&](uint32_t col, int kk) {
-                if (C::DQ_T)  // dQ^T = K^T dS^T
-                    umma_ss(tmem + col, dKm + mnmaj(kk), dDSm + mnmaj(kk), idDQ, kk > 0);
-                else  // dQ = dS K
-                    umma_ss(tmem + col, dDSm + mnmaj(kk), dKm + mnmaj(kk), idDQ, kk > 0);
-            };
-            bool ok = mbar_wait(bar_addr(bars->kv_full), 0, abort_flag, p.status, 50) && q_wait(0);
-            if constexpr (C::NSB == 2) {
-                // Per query tile i (consecutive MMAs alternate between independent GEMMs):
-                //   [P(i) ready]  dV(i) || S^T(i+1)          (different S^T buffers)
-                //   [dS(i) ready] dK(i) || dQ(i), then dQ(i) || dP^T(i+1)
-                // dP^T(i+1) overwrites dS^T(i): it starts after every dK(i) step.
-                if (ok) {
-                    tc_fence_after();
+            for (int it = 0; ok && it < n_it; ++it) {
+                const int st = it % C::QST, b = it % C::NSB;
+                const bool first = it == 0;
+                const uint32_t cS = C::C_S0 + (uint32_t)(b * BQ);
+                const uint64_t dQm = dQm0 + st * kStage, dDOm = dDOm0 + st * kStage;
+                if (!(ok = mbar_wait(bar_addr(bars->p_full), it & 1, abort_flag, p.status, 52))) break;
+                tc_fence_after();
 #pragma unroll
-                    for (int kk = 0; kk < NS; ++kk) {
-                        s_step(C::C_S0, dQk0, kk);
-                        dp_step(dDOk0, kk);
-                    }
-                    umma_commit(bar_addr(bars->s_full[0]));
-                    umma_commit(bar_addr(bars->dp_full));
+                for (int kk = 0; kk < NA; ++kk)  // dV += P^T dO
+                    umma_ts(tmem + C::C_DV, tmem + cS + acc_a(kk), dDOm + mnmaj(kk), idAcc,
+                            (first && kk == 0) ? 0u : 1u);
+                umma_commit(bar_addr(bars->sfree[b]));
+                if (!(ok = mbar_wait(bar_addr(bars->ds_full), it & 1, abort_flag, p.status, 54))) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < NA; ++kk)  // dK += dS^T Q
+                    umma_ts(tmem + C::C_DK, tmem + C::C_DP + acc_a(kk), dQm + mnmaj(kk), idAcc,
+                            (first && kk == 0) ? 0u : 1u);
+                umma_commit(bar_addr(bars->dpfree));
+                // Q(it) and dO(it) are read by nothing after dK(it): S^T(it) and
+                // dP^T(it) completed before dS(it) existed.
+                umma_commit(bar_addr(bars->q_empty[st]));
+                const int dqb = it % C::NDQ;
+                if (!(ok = mbar_wait(bar_addr(bars->dq_empty[dqb]), ((it / C::NDQ) & 1) ^ 1,
+                                     abort_flag, p.status, 55)))
+                    break;
+                tc_fence_after();
+                const uint32_t cq = C::C_DQ0 + (uint32_t)(dqb * C::DQ_COLS);
+#pragma unroll
+                for (int kk = 0; kk < NQ; ++kk) {
+                    if (C::DQ_T)  // dQ^T = K^T dS^T
+                        umma_ss(tmem + cq, dKm + mnmaj(kk), dDSm + mnmaj(kk), idDQ, kk > 0);
+                    else  // dQ = dS K
+                        umma_ss(tmem + cq, dDSm + mnmaj(kk), dKm + mnmaj(kk), idDQ, kk > 0);
                 }
-                for (int it = 0; ok && it < n_it; ++it) {
-                    const int st = it % C::QST, stn = (it + 1) % C::QST;
-                    const bool next = it + 1 < n_it;
-                    const uint64_t dQm = dQm0 + st * kStage, dDOm = dDOm0 + st * kStage;
-                    const uint64_t dQkn = dQk0 + stn * kStage, dDOkn = dDOk0 + stn * kStage;
-                    const uint32_t cS = s_col(it), cSn = s_col(it + 1);
-                    const bool first = it == 0;
-                    if (!(ok = mbar_wait(bar_addr(bars->p_full), it & 1, abort_flag, p.status, 52))) break;
-                    if (next && !(ok = q_wait(it + 1))) break;
-                    tc_fence_after();
-                    if (next) {
-#pragma unroll
-                        for (int kk = 0; kk < NS; ++kk) {
-                            if (kk < NA) acc_step(C::C_DV, cS, dDOm, kk, first);
-                            s_step(cSn, dQkn, kk);
-                        }
-                        umma_commit(bar_addr(bars->s_full[(it + 1) % 2]));
-                    } else {
-#pragma unroll
-                        for (int kk = 0; kk < NA; ++kk) acc_step(C::C_DV, cS, dDOm, kk, first);
-                    }
-                    if (!(ok = mbar_wait(bar_addr(bars->ds_full), it & 1, abort_flag, p.status, 54))) break;
-                    if (!(ok = mbar_wait(bar_addr(bars->dq_empty[0]), (it & 1) ^ 1, abort_flag,
-                                         p.status, 55)))
-                        break;
-                    tc_fence_after();
-#pragma unroll
-                    for (int kk = 0; kk < NA; ++kk) {
-                        acc_step(C::C_DK, C::C_DP, dQm, kk, first);
-                        dq_step(C::C_DQ0, kk);
-                    }
-                    if (next) {
-#pragma unroll
-                        for (int kk = 0; kk < NS; ++kk) {
-                            dp_step(dDOkn, kk);
-                            if (NA + kk < NQ) dq_step(C::C_DQ0, NA + kk);
-                        }
-                    } else {
-#pragma unroll
-                        for (int kk = NA; kk < NQ; ++kk) dq_step(C::C_DQ0, kk);
-                    }
-                    umma_commit(bar_addr(bars->dq_full[0]));
-                    umma_commit(bar_addr(bars->q_empty[st]));
-                    if (next) umma_commit(bar_addr(bars->dp_full));
-                }
-            } else {
-                // One S^T buffer: S^T(i+1) waits for dV(i) to read P^T(i).
-                if (ok) {
-                    tc_fence_after();
-#pragma unroll
-                    for (int kk = 0; kk < NS; ++kk) s_step(C::C_S0, dQk0, kk);
-                    umma_commit(bar_addr(bars->s_full[0]));
-#pragma unroll
-                    for (int kk = 0; kk < NS; ++kk) dp_step(dDOk0, kk);
-                    umma_commit(bar_addr(bars->dp_full));
-                }
-                for (int it = 0; ok && it < n_it; ++it) {
-                    const int st = it % C::QST, stn = (it + 1) % C::QST;
-                    const bool first = it == 0;
-                    const uint64_t dQm = dQm0 + st * kStage, dDOm = dDOm0 + st * kStage;
-                    if (!(ok = mbar_wait(bar_addr(bars->p_full), it & 1, abort_flag, p.status, 52))) break;
-                    tc_fence_after();
-#pragma unroll
-                    for (int kk = 0; kk < NA; ++kk) acc_step(C::C_DV, C::C_S0, dDOm, kk, first);
-                    if (it + 1 < n_it) {
-                        if (!(ok = q_wait(it + 1))) break;
-                        tc_fence_after();
-#pragma unroll
-                        for (int kk = 0; kk < NS; ++kk) s_step(C::C_S0, dQk0 + stn * kStage, kk);
-                        umma_commit(bar_addr(bars->s_full[0]));
-                    }
-                    if (!(ok = mbar_wait(bar_addr(bars->ds_full), it & 1, abort_flag, p.status, 54))) break;
-                    tc_fence_after();
-#pragma unroll
-                    for (int kk = 0; kk < NA; ++kk) acc_step(C::C_DK, C::C_DP, dQm, kk, first);
-                    const int dqb = it % C::NDQ;
-                    if (!(ok = mbar_wait(bar_addr(bars->dq_empty[dqb]), ((it / C::NDQ) & 1) ^ 1,
-                                         abort_flag, p.status, 55)))
-                        break;
-                    tc_fence_after();
-                    const uint32_t cq = C::C_DQ0 + (uint32_t)(dqb * C::DQ_COLS);
-#pragma unroll
-                    for (int kk = 0; kk < NQ; ++kk) dq_step(cq, kk);
-                    umma_commit(bar_addr(bars->dq_full[dqb]));
-                    umma_commit(bar_addr(bars->q_empty[st]));
-                    if (it + 1 < n_it) {
-#pragma unroll
-                        for (int kk = 0; kk < NS; ++kk) dp_step(dDOk0 + stn * kStage, kk);
-                        umma_commit(bar_addr(bars->dp_full));
-                    }
-                }
+                umma_commit(bar_addr(bars->dq_full[dqb]));
             }
             umma_commit(bar_addr(bars->acc_done));
             umma_commit(bar_addr(bars->done));
@@ -477,6 +431,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
 #pragma unroll
             for (int c = 0; c < HC / 2; c += 16) tmem_st16(tl + cD + c, pk + c);
+            // The smem dS tile is free once dQ(it - 1) (issued by the other MMA
+            // thread than dP^T(it)) has read it.
+            if (it > 0 && !(ok = mbar_wait(bar_addr(bars->dq_full[(it - 1) % C::NDQ]),
+                                           ((it - 1) / C::NDQ) & 1, abort_flag, p.status, 64)))
+                break;
             // smem: 16-byte piece u of the 128-byte row of 64-column chunk k holds
             // columns k*64 + 8u .. +7.
 #pragma unroll
