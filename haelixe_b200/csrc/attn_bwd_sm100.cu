@@ -49,7 +49,7 @@ template <int D>
 struct BCfg {
     static constexpr int BQ = D == 128 ? 64 : 128;  // queries per inner tile
     static constexpr bool DQ_T = D == 128;           // dQ computed transposed (M = D)
-    static constexpr int QST = 3;                    // Q/dO/lse/delta ring depth
+    static constexpr int QST = 2;                    // Q/dO/lse/delta ring depth
     static constexpr int REGS_CTL = D == 128 ? 104 : 64;
     static constexpr int REGS_COMPUTE = D == 128 ? 160 : 168;
     static constexpr int REGS_DRAIN = D == 128 ? 88 : 112;
@@ -61,17 +61,25 @@ struct BCfg {
     static constexpr int KT = BK * D * 2;
     static constexpr int QT = BQ * D * 2;
     static constexpr int DST = BK * BQ * 2;
+    // smem dS^T tiles: two for D=128, so dS(i+1) can be written while dK(i) and
+    // dQ(i) still read dS(i); D=64 has room for one.
+    static constexpr int NDS = D == 128 ? 2 : 1;
     static constexpr int K_OFF = 0;
     static constexpr int V_OFF = K_OFF + KT;
     static constexpr int Q_OFF = V_OFF + KT;
     static constexpr int DO_OFF = Q_OFF + QST * QT;
     static constexpr int DS_OFF = DO_OFF + QST * QT;
     static constexpr int DQS = BQ * D * 4;           // f32 dQ staging tile for the reduce-add
-    static constexpr int DQS_OFF = DS_OFF + DST;
-    static constexpr int LSE_OFF = DQS_OFF + DQS;
+    // Two staging tiles: the L2 reduce-add of one tile (~0.75 us for 32 KB at
+    // the chip's ~5.9 TB/s reduction rate, shared by all SMs) overlaps the
+    // drain of the next.
+    static constexpr int NDQS = 2;
+    static constexpr int DQS_OFF = DS_OFF + NDS * DST;
+    static constexpr int LSE_OFF = DQS_OFF + NDQS * DQS;
     static constexpr int DEL_OFF = LSE_OFF + QST * BQ * 4;
     static constexpr int BAR_OFF = DEL_OFF + QST * BQ * 4;
     static constexpr int SMEM = BAR_OFF + 256 + 1024;
+    static_assert(SMEM <= 232448, "shared memory per block");
     // TMEM columns. D=128: two S^T buffers (the next tile's K Q^T runs while P of
     // this one is computed) and one dQ^T buffer; D=64: one S^T buffer, two dQ.
     static constexpr int NSB = D == 128 ? 2 : 1;
@@ -85,8 +93,14 @@ struct BCfg {
 struct BBars {
     uint64_t kv_full;
     uint64_t q_full[4], q_empty[4];  // indexed by ring stage (QST <= 4)
-    uint64_t s_full[2], dp_full, p_full, ds_full;
-    uint64_t sfree[2], dpfree;  // TMEM hand-offs from the accumulate to the recompute issuer
+    uint64_t s_full[2], dp_full;
+    // P(i) / dS(i) ready, indexed by i & 1: the P/dS warpgroups can run up to
+    // two query tiles ahead of the accumulate issuer (S^T(i+1) does not wait
+    // for dV(i)), so one barrier per parity keeps every wait on its own phase.
+    uint64_t p_full[2], ds_full[2];
+    uint64_t sfree[2];          // S^T buffer b read by dV (accumulate -> recompute issuer)
+    uint64_t dpfree;            // dP^T columns loaded by the P/dS warpgroups (-> recompute issuer)
+    uint64_t dsfree[2];         // smem dS tile b read by dK and dQ (-> P/dS warpgroups)
     uint64_t dq_full[2], dq_empty[2];
     uint64_t dqs_free, dqs_full;
     uint64_t acc_done, done, done_r;
@@ -151,9 +165,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(bar_addr(bars->dp_full), 1);
         mbar_init(bar_addr(bars->sfree[0]), 1);
         mbar_init(bar_addr(bars->sfree[1]), 1);
-        mbar_init(bar_addr(bars->dpfree), 1);
-        mbar_init(bar_addr(bars->p_full), 256);
-        mbar_init(bar_addr(bars->ds_full), 256);
+        mbar_init(bar_addr(bars->dpfree), 256);
+        mbar_init(bar_addr(bars->dsfree[0]), 1);
+        mbar_init(bar_addr(bars->dsfree[1]), 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(bar_addr(bars->p_full[s]), 256);
+            mbar_init(bar_addr(bars->ds_full[s]), 256);
+        }
         for (int s = 0; s < 2; ++s) {
             mbar_init(bar_addr(bars->dq_full[s]), 1);
             mbar_init(bar_addr(bars->dq_empty[s]), 128);
@@ -235,9 +253,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // thread leaves the pipe idle during every mbarrier wait):
         //   warp 3 lane 0 (recompute): S^T(i) = K Q^T and dP^T(i) = V dO^T;
         //   warp 1 lane 0 (accumulate): dV += P^T dO, dK += dS^T Q, dQ(i).
-        // TMEM hand-offs between the two go through mbarriers committed by the
-        // thread whose MMAs free a buffer: sfree[b] after dV reads P^T from S
-        // buffer b, dpfree after dK reads dS^T from the dP^T columns.
+        // Buffer hand-offs go through mbarriers: sfree[b] (committed after dV
+        // read P^T from S buffer b), dpfree (the P/dS warpgroups have loaded
+        // dP^T into registers), dsfree[b] (dK and dQ read smem dS tile b).
         constexpr uint32_t idSP = idesc_bf16_f32(BK, BQ, false, false);
         constexpr uint32_t idAcc = idesc_bf16_f32(BK, D, false, true);
         constexpr uint32_t idDQ =
@@ -279,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kk = 0; kk < NS; ++kk)
                     umma_ss(tmem + cS, dKk + kmaj(kk, C::CHUNK_K), dq + kmaj(kk, C::CHUNK_Q), idSP, kk > 0);
                 umma_commit(bar_addr(bars->s_full[b]));
-                // The dP^T columns are free once dK(it - 1) has read dS^T(it - 1).
+                // The dP^T columns are free once the P/dS warpgroups loaded dP^T(it - 1).
                 if (!(ok = mbar_wait(bar_addr(bars->dpfree), (it & 1) ^ 1, abort_flag, p.status, 57)))
                     break;
                 tc_fence_after();
@@ -294,31 +312,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else if (warp == 1 && lane == 0) {
             // -------- accumulate issuer
             const uint64_t dKm = sdesc_sw128(sK, C::CHUNK_K, 1024);     // K, MN-major (dQ)
-            const uint64_t dDSm = sdesc_sw128(sDS, C::CHUNK_DS, 1024);  // dS, MN-major (dQ)
+            const uint64_t dDSm = sdesc_sw128(sDS, C::CHUNK_DS, 1024);  // dS tile 0, MN-major (dQ)
+            const uint64_t dDSk = sdesc_sw128(sDS, 16, 1024);           // dS tile 0, K-major (A of dK)
+            constexpr uint64_t kDsTile = (uint64_t)(C::DST >> 4);
             const uint64_t dQm0 = sdesc_sw128(sQ, C::CHUNK_Q, 1024);    // Q stage 0, MN-major
             const uint64_t dDOm0 = sdesc_sw128(sDO, C::CHUNK_Q, 1024);  // dO stage 0, MN-major
             // A column of dV/dK K-step kk: warpgroup g packed its BQ/2 columns at the
             // start of its own f32 columns [g*BQ/2, ...).
             auto acc_a = [](int kk) { return (uint32_t)((kk / KH) * (BQ / 2) + (kk % KH) * 8); };
             for (int it = 0; ok && it < n_it; ++it) {
-                const int st = it % C::QST, b = it % C::NSB;
+                const int st = it % C::QST, b = it % C::NSB, db = it % C::NDS;
                 const bool first = it == 0;
                 const uint32_t cS = C::C_S0 + (uint32_t)(b * BQ);
+                const uint64_t dsm = dDSm + db * kDsTile, dsk = dDSk + db * kDsTile;
                 const uint64_t dQm = dQm0 + st * kStage, dDOm = dDOm0 + st * kStage;
-                if (!(ok = mbar_wait(bar_addr(bars->p_full), it & 1, abort_flag, p.status, 52))) break;
+                if (!(ok = mbar_wait(bar_addr(bars->p_full[it & 1]), (it >> 1) & 1, abort_flag, p.status,
+                                     52)))
+                    break;
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < NA; ++kk)  // dV += P^T dO
                     umma_ts(tmem + C::C_DV, tmem + cS + acc_a(kk), dDOm + mnmaj(kk), idAcc,
                             (first && kk == 0) ? 0u : 1u);
                 umma_commit(bar_addr(bars->sfree[b]));
-                if (!(ok = mbar_wait(bar_addr(bars->ds_full), it & 1, abort_flag, p.status, 54))) break;
+                if (!(ok = mbar_wait(bar_addr(bars->ds_full[it & 1]), (it >> 1) & 1, abort_flag, p.status,
+                                     54)))
+                    break;
                 tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < NA; ++kk)  // dK += dS^T Q
-                    umma_ts(tmem + C::C_DK, tmem + C::C_DP + acc_a(kk), dQm + mnmaj(kk), idAcc,
+                for (int kk = 0; kk < NA; ++kk)  // dK += dS^T Q (dS^T K-major from smem)
+                    umma_ss(tmem + C::C_DK, dsk + kmaj(kk, C::CHUNK_DS), dQm + mnmaj(kk), idAcc,
                             (first && kk == 0) ? 0u : 1u);
-                umma_commit(bar_addr(bars->dpfree));
                 // Q(it) and dO(it) are read by nothing after dK(it): S^T(it) and
                 // dP^T(it) completed before dS(it) existed.
                 umma_commit(bar_addr(bars->q_empty[st]));
@@ -331,11 +355,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int kk = 0; kk < NQ; ++kk) {
                     if (C::DQ_T)  // dQ^T = K^T dS^T
-                        umma_ss(tmem + cq, dKm + mnmaj(kk), dDSm + mnmaj(kk), idDQ, kk > 0);
+                        umma_ss(tmem + cq, dKm + mnmaj(kk), dsm + mnmaj(kk), idDQ, kk > 0);
                     else  // dQ = dS K
-                        umma_ss(tmem + cq, dDSm + mnmaj(kk), dKm + mnmaj(kk), idDQ, kk > 0);
+                        umma_ss(tmem + cq, dsm + mnmaj(kk), dKm + mnmaj(kk), idDQ, kk > 0);
                 }
                 umma_commit(bar_addr(bars->dq_full[dqb]));
+                umma_commit(bar_addr(bars->dsfree[db]));
             }
             umma_commit(bar_addr(bars->acc_done));
             umma_commit(bar_addr(bars->done));
@@ -359,7 +384,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kr = k0 + r;
         const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
         const float sl2 = p.scale * kLog2e;
-        uint8_t* ds_row = sm + C::DS_OFF + r * 128;
         const int c0 = g * HC;  // first column of this warpgroup
         bool ok = true;
         for (int it = 0; it < n_it; ++it) {
@@ -409,16 +433,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < HC / 2; c += 16) tmem_st16(tl + cS + c, pk + c);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(bar_addr(bars->p_full));
+            mbar_arrive(bar_addr(bars->p_full[it & 1]));
 
             if (!(ok = mbar_wait(bar_addr(bars->dp_full), it & 1, abort_flag, p.status, 62))) break;
             tc_fence_after();
-            // dS^T = P^T (dP^T - delta) -> TMEM (over this warpgroup's dP columns) and
-            // the 128-byte-swizzled smem tile the dQ MMA reads.
+            // dS^T = P^T (dP^T - delta) -> the 128-byte-swizzled smem tile the dK
+            // and dQ MMAs read. The dP^T columns are released as soon as they are
+            // in registers, so dP^T(it + 1) overlaps the rest of this phase.
 #pragma unroll
             for (int c = 0; c < HC; c += 32) tmem_ld32(tl + cD + c, x + c);
             tmem_ld_wait();
             reg_fence<HC>(x);
+            tc_fence_before();
+            mbar_arrive(bar_addr(bars->dpfree));
 #pragma unroll
             for (int q4 = 0; q4 < HC / 4; ++q4) {
                 const float4 d4 = reinterpret_cast<const float4*>(del)[q4];
@@ -429,13 +456,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pk[2 * q4] = pack_bf16(a0, a1);
                 pk[2 * q4 + 1] = pack_bf16(a2, a3);
             }
-#pragma unroll
-            for (int c = 0; c < HC / 2; c += 16) tmem_st16(tl + cD + c, pk + c);
-            // The smem dS tile is free once dQ(it - 1) (issued by the other MMA
-            // thread than dP^T(it)) has read it.
-            if (it > 0 && !(ok = mbar_wait(bar_addr(bars->dq_full[(it - 1) % C::NDQ]),
-                                           ((it - 1) / C::NDQ) & 1, abort_flag, p.status, 64)))
+            // smem dS tile db is free once dK(it - NDS) and dQ(it - NDS) have read it.
+            const int db = it % C::NDS;
+            if (!(ok = mbar_wait(bar_addr(bars->dsfree[db]), ((it / C::NDS) & 1) ^ 1, abort_flag,
+                                 p.status, 64)))
                 break;
+            uint8_t* ds_row = sm + C::DS_OFF + db * C::DST + r * 128;
             // smem: 16-byte piece u of the 128-byte row of 64-column chunk k holds
             // columns k*64 + 8u .. +7.
 #pragma unroll
@@ -445,10 +471,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<uint4*>(ds_row + chunk * C::CHUNK_DS + ((u ^ (r & 7)) * 16)) =
                     make_uint4(pk[4 * u8], pk[4 * u8 + 1], pk[4 * u8 + 2], pk[4 * u8 + 3]);
             }
-            tmem_st_wait();
             fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
-            tc_fence_before();
-            mbar_arrive(bar_addr(bars->ds_full));
+            mbar_arrive(bar_addr(bars->ds_full[it & 1]));
         }
         // Epilogue: warpgroup 0 stores dV, warpgroup 1 stores dK (times scale).
         if (ok && mbar_wait(bar_addr(bars->acc_done), 0, abort_flag, p.status, 63)) {
@@ -489,9 +513,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = wi * 32 + lane;  // TMEM lane: d (dQ^T) or query row (dQ)
         const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
         const bool elected = (warp == 12 && lane == 0);
-        float* stage = (float*)(sm + C::DQS_OFF);
         for (int it = 0; it < n_it; ++it) {
             const int buf = it % C::NDQ;
+            float* stage = (float*)(sm + C::DQS_OFF + (it % C::NDQS) * C::DQS);
             const int q0 = (i_start + it) * BQ;
             if (!mbar_wait(bar_addr(bars->dq_full[buf]), (it / C::NDQ) & 1, abort_flag, p.status, 70)) break;
             tc_fence_after();
@@ -501,9 +525,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             reg_fence<C::DQ_COLS>(v);
             tc_fence_before();
             mbar_arrive(bar_addr(bars->dq_empty[buf]));
-            // The previous reduce-add must have read the staging tile.
+            // The reduce-add that used this staging tile (NDQS tiles ago) must
+            // have read it; the NDQS - 1 later ones may still be in flight.
             if (elected) {
-                bulk_wait_group_read0();
+                bulk_wait_group_read<C::NDQS - 1>();
                 mbar_arrive(bar_addr(bars->dqs_free));
             }
             if (!mbar_wait(bar_addr(bars->dqs_free), it & 1, abort_flag, p.status, 71)) break;

@@ -149,6 +149,12 @@ __device__ __forceinline__ void bulk_commit_group() {
 __device__ __forceinline__ void bulk_wait_group_read0() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// Waits until at most N of this thread's committed bulk groups still have to
+// read their smem sources.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
 // Waits until this thread's committed bulk groups completed.
 __device__ __forceinline__ void bulk_wait_group0() {
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
