@@ -12,18 +12,20 @@
 //           dP^T = V dO^T     (SS UMMA)                         -> TMEM
 //           P^T  = exp2(S^T * scale*log2e - lse*log2e) (mask)   -> TMEM (bf16)
 //           dV  += P^T dO     (TS UMMA, A from TMEM, B = dO MN-major)
-//           dS^T = P^T (dP^T - delta)                           -> TMEM + smem (bf16)
-//           dK  += dS^T Q     (TS UMMA)
-//           dQ   = dS K       (SS UMMA from the smem copy of dS; for D=128 as
-//                              dQ^T = K^T dS^T so M = D = 128)  -> TMEM (2 buffers)
-//         a second warpgroup drains each dQ tile from TMEM into the f32
-//         accumulator with atomics while the tensor core moves on;
+//           dS^T = P^T (dP^T - delta)                           -> smem (bf16)
+//           dK  += dS^T Q     (SS UMMA, dS^T K-major from smem)
+//           dQ   = dS K       (SS UMMA from the smem dS tile; for D=128 as
+//                              dQ^T = K^T dS^T so M = D = 128)  -> TMEM
+//         a drain warpgroup moves each dQ tile TMEM -> registers -> an f32
+//         smem staging tile, and one thread adds it into the accumulator with
+//         a bulk tensor reduce-add while the tensor core moves on;
 //   post  dQ = bf16(scale * accumulator), dK already carries the scale.
 // The scale on dQ and dK is the factor the reference's backward omits
 // (flash_attention.rs:31,34-36).
 //
 // Warp roles of `main` (512 threads): warp 0 TMA producer (Q, dO tiles and
-// the lse/delta rows of each query tile), warp 1 MMA issuer (one thread),
+// the lse/delta rows of each query tile), warp 1 lane 0 the accumulate MMA
+// issuer (dV, dK, dQ), warp 3 lane 0 the recompute MMA issuer (S^T, dP^T),
 // warp 2 TMEM allocator, warps 4-7 and 8-11 two P/dS warpgroups that split
 // each query tile's columns (thread = key row = TMEM lane), warps 12-15 the
 // dQ drain warpgroup. All mbarrier waits are bounded (sm100_ptx.cuh).
