@@ -2,8 +2,8 @@
 
 Workload (default): LLaMA-3-8B-shaped attention layer, bf16, B=4, H=32,
 S=8192, D=128, causal, RoPE (theta 500000) on Q and K before attention.
-One step = RoPE(Q), RoPE(K), attention forward, attention backward,
-RoPE backward of dQ and dK; with N GPUs the heads are sharded (H/N per rank)
+One step = RoPE(Q), RoPE(K), attention forward, attention backward with the
+RoPE backward of dQ and dK fused into it; with N GPUs the heads are sharded (H/N per rank)
 and the per-rank output shards are all-gathered over NCCL and reassembled
 into [B, S, H, D] (the merged-heads layout) on every rank.
 
@@ -302,7 +302,7 @@ def run_haelixe(a):
     qr, kr = torch.empty_like(q), torch.empty_like(k)
     o = torch.empty_like(q)
     lse = torch.empty(B * Hl * S, device=dev, dtype=torch.float32)
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+    dv = torch.empty_like(q)
     dq0, dk0 = torch.empty_like(q), torch.empty_like(q)
     if world > 1:
         gathered = torch.empty(world * B * Hl * S * D, device=dev, dtype=torch.bfloat16)
@@ -329,11 +329,12 @@ def run_haelixe(a):
             comm.wait_event(done)
             with torch.cuda.stream(comm):
                 dist.all_gather_into_tensor(gathered, o.reshape(-1))
-        hx.attn_backward(qr, kr, v, o, lse, do, scale, causal, dq=dq, dk=dk, dv=dv)
+        # Backward with the rotary embedding's backward fused into the last
+        # writes of dQ and dK: dq0, dk0 are the gradients of q, k before RoPE.
+        hx.attn_backward(qr, kr, v, o, lse, do, scale, causal, dq=dq0, dk=dk0, dv=dv,
+                         rope_base=a.rope_theta)
         if timed:
             ev["b1"][-1].record(stream)
-        hx.rope_backward(dq, a.rope_theta, out=dq0)
-        hx.rope_backward(dk, a.rope_theta, out=dk0)
         if world > 1:
             stream.wait_stream(comm)
             N.check(N.lib().hx_reassemble_heads(ctx.handle, N.HX_BF16, gathered.data_ptr(),

@@ -82,6 +82,8 @@ SIGNATURES = {
     "hx_attn_fwd_strided": (_I, [_P, _I, _SHP, _P, _P, _P, _P, _P, _F, _I]),
     "hx_attn_bwd_strided": (_I, [_P, _I, _SHP, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _U64,
                                  _F, _I]),
+    "hx_attn_bwd_rope_strided": (_I, [_P, _I, _SHP, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                      _U64, _F, _I, _F]),
     "hx_rope_fwd": (_I, [_P, _I, _SHP, _P, _P, _F]),
     "hx_rope_bwd": (_I, [_P, _I, _SHP, _P, _P, _F]),
     "hx_reassemble_heads": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _I, _I]),

@@ -163,8 +163,13 @@ def attn_forward(q, k, v, scale: float, causal: bool = False, out=None, lse=None
 
 
 def attn_backward(q, k, v, o, lse, dout, scale: float, causal: bool = False,
-                  dq=None, dk=None, dv=None):
-    """Runs the fused backward. Returns (dq, dk, dv)."""
+                  dq=None, dk=None, dv=None, rope_base: Optional[float] = None):
+    """Runs the fused backward. Returns (dq, dk, dv).
+
+    With rope_base, q and k are the rotary-embedded tensors the forward used and
+    dq, dk are returned with respect to the tensors before the rotation
+    (rope_backward fused into the backward's last writes of dq and dk).
+    """
     dout = dout if dout.stride() == q.stride() else dout.contiguous()
     _check_operands(q, k, v, o, dout)
     ctx = context(q.device.index)
@@ -173,19 +178,32 @@ def attn_backward(q, k, v, o, lse, dout, scale: float, causal: bool = False,
     dq = torch.empty_like(q) if dq is None else dq
     dk = torch.empty_like(q) if dk is None else dk
     dv = torch.empty_like(q) if dv is None else dv
-    N.check(N.lib().hx_attn_bwd_strided(ctx.handle, _DTYPES[q.dtype], ctypes.byref(shp),
-                                        _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dout),
-                                        _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv), None, 0,
-                                        float(scale), int(bool(causal))), ctx.handle)
+    if rope_base is None:
+        N.check(N.lib().hx_attn_bwd_strided(ctx.handle, _DTYPES[q.dtype], ctypes.byref(shp),
+                                            _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dout),
+                                            _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv), None, 0,
+                                            float(scale), int(bool(causal))), ctx.handle)
+    else:
+        N.check(N.lib().hx_attn_bwd_rope_strided(ctx.handle, _DTYPES[q.dtype], ctypes.byref(shp),
+                                                 _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dout),
+                                                 _ptr(lse), _ptr(dq), _ptr(dk), _ptr(dv), None, 0,
+                                                 float(scale), int(bool(causal)),
+                                                 float(rope_base)), ctx.handle)
     return dq, dk, dv
 
 
 class FlashAttentionOp:
-    """Autograd node of the fused attention (src/ops/flash_attention.rs:3-40)."""
+    """Autograd node of the fused attention (src/ops/flash_attention.rs:3-40).
 
-    def __init__(self, q, k, v, scale: float, o, lse, causal: bool = False):
+    With rope_base set, q and k held here are the rotated tensors and the
+    gradients returned are those of the tensors before the rotation.
+    """
+
+    def __init__(self, q, k, v, scale: float, o, lse, causal: bool = False,
+                 rope_base: Optional[float] = None):
         self.q, self.k, self.v, self.scale = q, k, v, float(scale)
         self.o, self.lse, self.causal = o, lse, bool(causal)
+        self.rope_base = rope_base
 
     def name(self) -> str:
         return "FlashAttention"
@@ -193,34 +211,42 @@ class FlashAttentionOp:
     def backward(self, grad_out: torch.Tensor) -> list:
         """Gradients for the parents in the order [q, k, v] (ops/flash_attention.rs:38)."""
         dq, dk, dv = attn_backward(self.q, self.k, self.v, self.o, self.lse, grad_out,
-                                   self.scale, self.causal)
+                                   self.scale, self.causal, rope_base=self.rope_base)
         return [dq, dk, dv]
 
 
 class _FlashAttentionFn(torch.autograd.Function):
     @staticmethod
-    def forward(fctx, q, k, v, scale, causal):
-        o, lse = attn_forward(q.detach(), k.detach(), v.detach(), scale, causal)
-        fctx.op = FlashAttentionOp(q.detach(), k.detach(), v.detach(), scale, o, lse, causal)
+    def forward(fctx, q, k, v, scale, causal, rope_base):
+        q, k = q.detach(), k.detach()
+        if rope_base is not None:
+            q, k = rope_forward(q, rope_base), rope_forward(k, rope_base)
+        o, lse = attn_forward(q, k, v.detach(), scale, causal)
+        fctx.op = FlashAttentionOp(q, k, v.detach(), scale, o, lse, causal, rope_base)
         return o
 
     @staticmethod
     def backward(fctx, grad_out):
         dq, dk, dv = fctx.op.backward(grad_out)
-        return dq, dk, dv, None, None
+        return dq, dk, dv, None, None, None
 
 
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
-                    causal: bool = False) -> torch.Tensor:
+                    causal: bool = False, rope_base: Optional[float] = None) -> torch.Tensor:
     """softmax(scale * q k^T [causal]) v on CUDA (Tensor::flash_attention, tensor.rs:644).
 
     q, k, v: [B*H, S, D] (the reference's layout) or [B, H, S, D] views with a
     contiguous head dim; f32 or bf16. When any input requires grad, the result
     carries a FlashAttentionOp node, as `with_node` does in the reference
-    (tensor.rs:655-663).
+    (tensor.rs:655-663). With rope_base, q and k are rotated first (the order of
+    MultiHeadAttention::forward, nn/attention.rs:76-78) and the backward returns
+    their gradients before the rotation.
     """
     if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
-        return _FlashAttentionFn.apply(q, k, v, float(scale), bool(causal))
+        return _FlashAttentionFn.apply(q, k, v, float(scale), bool(causal),
+                                       None if rope_base is None else float(rope_base))
+    if rope_base is not None:
+        q, k = rope_forward(q, rope_base), rope_forward(k, rope_base)
     o, _ = attn_forward(q, k, v, scale, causal)
     return o
 

@@ -122,8 +122,20 @@ struct BwdParams {
     int S, H;
     float scale;
     int causal;
+    // (cos, sin) of s * base^(-2i/D) for [S][D/2], or null. When set, dK leaves
+    // the kernel rotated back by -theta of its key row: the gradient with
+    // respect to K before the rotary embedding (src/kernels/rope.rs:44-82).
+    const float2* rope_tab;
     DeviceStatus* status;
 };
+
+// Rotation of one (x0, x1) pair by -theta with the reference's unfused
+// products and sums (src/kernels/rope.rs:37-38, 67): one rounding per
+// operation, no FMA contraction.
+__device__ __forceinline__ void rope_rot_back(float x0, float x1, float2 cs, float& y0, float& y1) {
+    y0 = __fadd_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+    y1 = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x0, cs.y));
+}
 
 __device__ __forceinline__ uint32_t bar_addr(const uint64_t& b) { return smem_addr(&b); }
 
@@ -484,13 +496,39 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t col = g ? C::C_DK : C::C_DV;
             const float mul = g ? p.scale : 1.f;
             __nv_bfloat16* dst = (g ? p.dk : p.dv) + off;
+            const bool rope = g == 1 && p.rope_tab != nullptr;
+            const float4* tab4 = reinterpret_cast<const float4*>(p.rope_tab + (int64_t)kr * (D / 2));
 #pragma unroll
             for (int c = 0; c < D; c += 32) {
                 uint32_t v[32];
                 tmem_ld32(tl + col + c, v);
                 tmem_ld_wait();
                 reg_fence<32>(v);
-                if (store) {
+                if (store && rope) {  // dK: pairs (c+2i, c+2i+1) rotated by -theta(kr)
+#pragma unroll
+                    for (int i2 = 0; i2 < 8; ++i2) {
+                        const float4 t = __ldg(tab4 + c / 4 + i2);  // pairs c/2+2*i2, +1
+                        float y0, y1, y2, y3;
+                        rope_rot_back(__uint_as_float(v[4 * i2]) * mul, __uint_as_float(v[4 * i2 + 1]) * mul,
+                                      make_float2(t.x, t.y), y0, y1);
+                        rope_rot_back(__uint_as_float(v[4 * i2 + 2]) * mul, __uint_as_float(v[4 * i2 + 3]) * mul,
+                                      make_float2(t.z, t.w), y2, y3);
+                        v[4 * i2] = __float_as_uint(y0);
+                        v[4 * i2 + 1] = __float_as_uint(y1);
+                        v[4 * i2 + 2] = __float_as_uint(y2);
+                        v[4 * i2 + 3] = __float_as_uint(y3);
+                    }
+                    uint4* d4 = reinterpret_cast<uint4*>(dst + c);
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        uint4 o;
+                        o.x = pack_bf16(__uint_as_float(v[8 * q4 + 0]), __uint_as_float(v[8 * q4 + 1]));
+                        o.y = pack_bf16(__uint_as_float(v[8 * q4 + 2]), __uint_as_float(v[8 * q4 + 3]));
+                        o.z = pack_bf16(__uint_as_float(v[8 * q4 + 4]), __uint_as_float(v[8 * q4 + 5]));
+                        o.w = pack_bf16(__uint_as_float(v[8 * q4 + 6]), __uint_as_float(v[8 * q4 + 7]));
+                        d4[q4] = o;
+                    }
+                } else if (store) {
                     uint4* d4 = reinterpret_cast<uint4*>(dst + c);
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
@@ -629,7 +667,7 @@ __global__ void __launch_bounds__(256) bwd_pre_kernel(const __nv_bfloat16* __res
 template <int D>
 __global__ void __launch_bounds__(256) bwd_post_kernel(const float* __restrict__ dq_acc,
                                                        __nv_bfloat16* __restrict__ dq, AttnDims d,
-                                                       float scale) {
+                                                       float scale, const float2* __restrict__ rope_tab) {
     const int64_t n8 = (int64_t)d.B * d.H * d.S * (D / 8);
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -640,11 +678,21 @@ __global__ void __launch_bounds__(256) bwd_post_kernel(const float* __restrict__
         const int hi = (int)(bhi % d.H), bi = (int)(bhi / d.H);
         const float4* src = reinterpret_cast<const float4*>(dq_acc + r * D + c8 * 8);
         const float4 a = src[0], c = src[1];
+        float y[8] = {a.x * scale, a.y * scale, a.z * scale, a.w * scale,
+                      c.x * scale, c.y * scale, c.z * scale, c.w * scale};
+        if (rope_tab != nullptr) {  // dQ rotated back by -theta(s): pairs 4*c8 .. 4*c8+3
+            const float4* t4 = reinterpret_cast<const float4*>(rope_tab + (int64_t)s * (D / 2) + 4 * c8);
+            const float4 t01 = t4[0], t23 = t4[1];
+            const float2 cs[4] = {make_float2(t01.x, t01.y), make_float2(t01.z, t01.w),
+                                  make_float2(t23.x, t23.y), make_float2(t23.z, t23.w)};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) rope_rot_back(y[2 * k], y[2 * k + 1], cs[k], y[2 * k], y[2 * k + 1]);
+        }
         uint4 o;
-        o.x = ptx::pack_bf16(a.x * scale, a.y * scale);
-        o.y = ptx::pack_bf16(a.z * scale, a.w * scale);
-        o.z = ptx::pack_bf16(c.x * scale, c.y * scale);
-        o.w = ptx::pack_bf16(c.z * scale, c.w * scale);
+        o.x = ptx::pack_bf16(y[0], y[1]);
+        o.y = ptx::pack_bf16(y[2], y[3]);
+        o.z = ptx::pack_bf16(y[4], y[5]);
+        o.w = ptx::pack_bf16(y[6], y[7]);
         *reinterpret_cast<uint4*>(dq + (int64_t)bi * d.sb + (int64_t)hi * d.sh + (int64_t)s * d.ss +
                                   c8 * 8) = o;
     }
@@ -675,7 +723,7 @@ template <int D>
 cudaError_t launch(cudaStream_t st, int sm_count, DeviceStatus* status, const AttnDims& d,
                    const void* q, const void* k, const void* v, const void* o, const void* dout,
                    const float* lse, void* dq, void* dk, void* dv, void* ws, float scale,
-                   int causal) {
+                   int causal, const float2* rope_tab) {
     using C = BCfg<D>;
     const BwdWorkspace w = carve(ws, d);
     const int64_t rows_pad = (int64_t)d.B * d.H * w.S_pad;
@@ -725,6 +773,7 @@ cudaError_t launch(cudaStream_t st, int sm_count, DeviceStatus* status, const At
     prm.H = d.H;
     prm.scale = scale;
     prm.causal = causal;
+    prm.rope_tab = rope_tab;
     prm.status = status;
     dim3 grid((d.S + BK - 1) / BK, d.H, d.B);
     attn_bwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, tdo, tdq, prm);
@@ -735,7 +784,7 @@ cudaError_t launch(cudaStream_t st, int sm_count, DeviceStatus* status, const At
     const int64_t n8 = (int64_t)d.B * d.H * d.S * (D / 8);
     int64_t blocks = (n8 + 255) / 256;
     if (blocks > (int64_t)sm_count * 32) blocks = (int64_t)sm_count * 32;
-    bwd_post_kernel<D><<<(unsigned)blocks, 256, 0, st>>>(w.dq_acc, (__nv_bfloat16*)dq, d, scale);
+    bwd_post_kernel<D><<<(unsigned)blocks, 256, 0, st>>>(w.dq_acc, (__nv_bfloat16*)dq, d, scale, rope_tab);
     note_launch();
     return cudaGetLastError();
 }
@@ -755,13 +804,14 @@ uint64_t sm100_bwd_workspace_bytes(const AttnDims& d) {
 cudaError_t sm100_attn_bwd(cudaStream_t st, int sm_count, DeviceStatus* status,
                            const AttnDims& d, const void* q, const void* k, const void* v,
                            const void* o, const void* dout, const float* lse, void* dq, void* dk,
-                           void* dv, void* workspace, float scale, int causal) {
+                           void* dv, void* workspace, float scale, int causal,
+                           const float2* rope_tab) {
     if (d.D == 64)
         return launch<64>(st, sm_count, status, d, q, k, v, o, dout, lse, dq, dk, dv, workspace,
-                          scale, causal);
+                          scale, causal, rope_tab);
     if (d.D == 128)
         return launch<128>(st, sm_count, status, d, q, k, v, o, dout, lse, dq, dk, dv, workspace,
-                           scale, causal);
+                           scale, causal, rope_tab);
     return cudaErrorInvalidValue;
 }
 

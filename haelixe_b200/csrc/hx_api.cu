@@ -402,19 +402,50 @@ int hx_attn_bwd_workspace_size(hx_dtype dt, const hx_attn_shape* shape, uint64_t
     return HX_OK;
 }
 
+static int rope_table_for(hx_ctx* c, const hx_attn_shape* shape, float base, float2** out,
+                          const char* who);
+static int attn_bwd_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* q,
+                           const void* k, const void* v, const void* o, const void* dout,
+                           const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                           uint64_t workspace_bytes, float scale, int causal, const float* rope_base);
+
 int hx_attn_bwd_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* q,
                         const void* k, const void* v, const void* o, const void* dout,
                         const float* lse, void* dq, void* dk, void* dv, void* workspace,
                         uint64_t workspace_bytes, float scale, int causal) {
+    return attn_bwd_common(c, dt, shape, q, k, v, o, dout, lse, dq, dk, dv, workspace,
+                           workspace_bytes, scale, causal, nullptr);
+}
+
+int hx_attn_bwd_rope_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* q,
+                             const void* k, const void* v, const void* o, const void* dout,
+                             const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                             uint64_t workspace_bytes, float scale, int causal, float rope_base) {
+    return attn_bwd_common(c, dt, shape, q, k, v, o, dout, lse, dq, dk, dv, workspace,
+                           workspace_bytes, scale, causal, &rope_base);
+}
+
+static int attn_bwd_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* q,
+                           const void* k, const void* v, const void* o, const void* dout,
+                           const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                           uint64_t workspace_bytes, float scale, int causal, const float* rope_base) {
     if (c == nullptr) return HX_ERR_INVALID;
     int st;
     if ((st = validate_dtype(c, dt, "hx_attn_bwd")) || (st = validate_shape(c, shape, "hx_attn_bwd")))
         return st;
+    float2* tab = nullptr;
+    if (rope_base != nullptr) {
+        if (shape->D % 2) return set_error(c, HX_ERR_INVALID, "hx_attn_bwd_rope: head_dim must be even");
+        if (!isfinite(*rope_base) || *rope_base <= 0.f)
+            return set_error(c, HX_ERR_INVALID, "hx_attn_bwd_rope: base must be positive and finite");
+    }
     if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv)
         return set_error(c, HX_ERR_INVALID, "hx_attn_bwd: NULL operand");
     if (!isfinite(scale)) return set_error(c, HX_ERR_INVALID, "hx_attn_bwd: scale is not finite");
     DeviceGuard g(c->device);
     LaunchCount lc(c);
+    if (rope_base != nullptr && (st = rope_table_for(c, shape, *rope_base, &tab, "hx_attn_bwd_rope")))
+        return st;
     const hx::AttnDims d = hx::dims_of(*shape);
     const bool fast = !c->force_simt && hx::sm100_bwd_supported(dt, d) &&
                       tma_layout_ok(d, {q, k, v, o, dout, dq, dk, dv});
@@ -432,12 +463,18 @@ int hx_attn_bwd_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, cons
     }
     cudaError_t e;
     if (fast) {
+        // With a rotary table the kernel's last writes of dK (main kernel) and
+        // dQ (post kernel) rotate them back: no extra pass over either.
         e = hx::sm100_attn_bwd(c->stream, c->sm_count, c->status, d, q, k, v, o, dout, lse, dq, dk,
-                               dv, ws, scale, causal);
+                               dv, ws, scale, causal, tab);
         c->last_path = 2;
     } else {
         e = hx::simt_attn_bwd(c->stream, dt, d, q, k, v, o, dout, lse, dq, dk, dv, (float*)ws,
                               scale, causal);
+        if (e == cudaSuccess && tab != nullptr) {  // SIMT path: separate in-place rotations
+            e = hx::rope_apply(c->stream, c->sm_count, dt, d, dq, dq, tab, -1.f);
+            if (e == cudaSuccess) e = hx::rope_apply(c->stream, c->sm_count, dt, d, dk, dk, tab, -1.f);
+        }
         c->last_path = 1;
     }
     st = check_cuda(c, e, fast ? "attention backward (tcgen05)" : "attention backward (SIMT)");
@@ -475,17 +512,11 @@ int hx_flash_attention_bwd(hx_ctx* c, hx_dtype dt, const void* q, const void* k,
 
 // ---- RoPE -----------------------------------------------------------------------------
 
-static int rope_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* x,
-                       void* out, float base, float sign, const char* who) {
-    if (c == nullptr) return HX_ERR_INVALID;
+// The (cos, sin) table of (S, D, base), built on first use and cached in the
+// context. Caller holds a DeviceGuard.
+static int rope_table_for(hx_ctx* c, const hx_attn_shape* shape, float base, float2** out,
+                          const char* who) {
     int st;
-    if ((st = validate_dtype(c, dt, who)) || (st = validate_shape(c, shape, who))) return st;
-    if (!x || !out) return set_error(c, HX_ERR_INVALID, "%s: NULL operand", who);
-    if (shape->D % 2) return set_error(c, HX_ERR_INVALID, "%s: head_dim must be even", who);
-    if (!isfinite(base) || base <= 0.f)
-        return set_error(c, HX_ERR_INVALID, "%s: base must be positive and finite", who);
-    DeviceGuard g(c->device);
-    LaunchCount lc(c);
     uint32_t base_bits;
     memcpy(&base_bits, &base, 4);
     float2* tab = nullptr;
@@ -515,6 +546,23 @@ static int rope_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const
             c->rope_tables.push_back({shape->S, shape->D, base_bits, tab});
         }
     }
+    *out = tab;
+    return HX_OK;
+}
+
+static int rope_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* x,
+                       void* out, float base, float sign, const char* who) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, who)) || (st = validate_shape(c, shape, who))) return st;
+    if (!x || !out) return set_error(c, HX_ERR_INVALID, "%s: NULL operand", who);
+    if (shape->D % 2) return set_error(c, HX_ERR_INVALID, "%s: head_dim must be even", who);
+    if (!isfinite(base) || base <= 0.f)
+        return set_error(c, HX_ERR_INVALID, "%s: base must be positive and finite", who);
+    DeviceGuard g(c->device);
+    LaunchCount lc(c);
+    float2* tab = nullptr;
+    if ((st = rope_table_for(c, shape, base, &tab, who))) return st;
     return check_cuda(c, hx::rope_apply(c->stream, c->sm_count, dt, hx::dims_of(*shape), x, out, tab, sign),
                       who);
 }

@@ -89,7 +89,8 @@ uint64_t sm100_bwd_workspace_bytes(const AttnDims& d);
 cudaError_t sm100_attn_bwd(cudaStream_t st, int sm_count, DeviceStatus* status,
                            const AttnDims& d, const void* q, const void* k, const void* v,
                            const void* o, const void* dout, const float* lse, void* dq,
-                           void* dk, void* dv, void* workspace, float scale, int causal);
+                           void* dk, void* dv, void* workspace, float scale, int causal,
+                           const float2* rope_tab = nullptr);
 
 // ---- head reassembly (heads.cu) ----
 cudaError_t reassemble_heads(cudaStream_t st, int elem_bytes, const void* src, void* dst, int n,

@@ -27,6 +27,9 @@
  *                                        (src/nn/attention.rs:62-73,91-94)
  *   hx_rope_fwd / hx_rope_bwd         <- rope_forward / rope_backward
  *                                        (src/kernels/rope.rs:5-82)
+ *   hx_attn_bwd_rope_strided          <- FlashAttentionOp::backward followed by
+ *                                        rope_backward of dq and dk (the rope ->
+ *                                        attention order of src/nn/attention.rs:76-78)
  *
  * Error behaviour: every entry point returns 0 (HX_OK) or a negative
  * hx_status. The reference panics instead (e.g. src/tensor.rs:652,
@@ -170,6 +173,17 @@ int hx_attn_bwd_strided(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape,
                         const void* k, const void* v, const void* o, const void* dout,
                         const float* lse, void* dq, void* dk, void* dv, void* workspace,
                         uint64_t workspace_bytes, float scale, int causal);
+
+/* hx_attn_bwd_strided for attention applied to rotary-embedded q and k (the
+ * order of MultiHeadAttention::forward, src/nn/attention.rs:76-78): q and k are
+ * the rotated tensors the forward used, and dq, dk come back as gradients with
+ * respect to the tensors before the rotation, i.e. hx_rope_bwd with rope_base
+ * already applied (rope_backward, src/kernels/rope.rs:44-82). On the tcgen05
+ * path the inverse rotation is part of the kernels' last writes of dk and dq. */
+int hx_attn_bwd_rope_strided(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape, const void* q,
+                             const void* k, const void* v, const void* o, const void* dout,
+                             const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                             uint64_t workspace_bytes, float scale, int causal, float rope_base);
 
 /* ---- rotary embedding (src/kernels/rope.rs) ---------------------------------- */
 /* Rotates interleaved pairs (2i, 2i+1) of every [.., S, D] row by

@@ -209,6 +209,61 @@ def test_reassemble_heads_kernel(dtype, layout):
     assert torch.equal(out, ref)
 
 
+ROPE_CASES = [(2, 255, 128), (1, 384, 128), (3, 128, 64), (2, 300, 64), (1, 97, 32)]
+
+
+def _rope_oracle(q0, k0, v, do, scale, causal, base, dtype):
+    """Rotate q, k (stored at the I/O precision), attention, rotate dq, dk back."""
+    qr, kr = ora.rope_fwd(q0, base), ora.rope_fwd(k0, base)
+    if dtype == torch.bfloat16:
+        qr, kr = ora.round_bf16(qr), ora.round_bf16(kr)
+    rdq, rdk, rdv = ora.attn_bwd(qr, kr, v, do, scale, causal)
+    return ora.rope_bwd(rdq, base), ora.rope_bwd(rdk, base), rdv
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("BH,S,D", ROPE_CASES)
+def test_fused_rope_backward_matches_oracle(BH, S, D, causal, dtype):
+    """hx_attn_bwd_rope_strided: gradients with respect to q, k before the rotation."""
+    base = 10000.0
+    seed = 7000 + BH * 100 + S + D
+    q0, k0, v, do = (_host((BH, S, D), seed + i, dtype) for i in range(4))
+    scale = 1.0 / math.sqrt(D)
+    ctx = hx.context()
+    expect = "tcgen05" if (dtype == torch.bfloat16 and D in (64, 128)) else "simt"
+    qd, kd = hx.rope_forward(_dev(q0, dtype), base), hx.rope_forward(_dev(k0, dtype), base)
+    vd, dod = _dev(v, dtype), _dev(do, dtype)
+    o, lse = hx.attn_forward(qd, kd, vd, scale, causal)
+    dq, dk, dv = hx.attn_backward(qd, kd, vd, o, lse, dod, scale, causal, rope_base=base)
+    assert ctx.last_path == expect
+    torch.cuda.synchronize()
+    rdq, rdk, rdv = _rope_oracle(q0, k0, v, do, scale, causal, base, dtype)
+    _check("dQ", dq, rdq, dtype)
+    _check("dK", dk, rdk, dtype)
+    _check("dV", dv, rdv, dtype)
+    # the fused rotation agrees with the separate rope_backward pass
+    g = hx.attn_backward(qd, kd, vd, o, lse, dod, scale, causal)
+    sep = (hx.rope_backward(g[0], base), hx.rope_backward(g[1], base))
+    for fused, ref in zip((dq, dk), sep):
+        a, b = fused.float().cpu().numpy(), ref.float().cpu().numpy()
+        assert (np.abs(a - b) <= 2 * _bf16_tol(b, 1e-3 if dtype == torch.float32 else 1e-2)).all()
+
+
+def test_autograd_node_with_rope():
+    """flash_attention(..., rope_base): rotation, attention and the fused backward."""
+    BH, S, D, base = 2, 200, 128, 500000.0
+    q0, k0, v, do = (_host((BH, S, D), 900 + i, torch.bfloat16) for i in range(4))
+    scale = 1.0 / math.sqrt(D)
+    qd, kd, vd = (_dev(a, torch.bfloat16).requires_grad_() for a in (q0, k0, v))
+    o = hx.flash_attention(qd, kd, vd, scale, causal=True, rope_base=base)
+    o.backward(_dev(do, torch.bfloat16))
+    rdq, rdk, rdv = _rope_oracle(q0, k0, v, do, scale, True, base, torch.bfloat16)
+    _check("dQ", qd.grad, rdq, torch.bfloat16)
+    _check("dK", kd.grad, rdk, torch.bfloat16)
+    _check("dV", vd.grad, rdv, torch.bfloat16)
+
+
 def _sampled_full_size(B, H, S, D, causal, rope_base=None, samples=((0, 0),)):
     """Full-size run on the GPU; oracle on sampled (b, h) slices; identities on all."""
     torch.manual_seed(0)
