@@ -1,8 +1,10 @@
 """haelixe_b200: B200-native (sm_100a) fused attention for the haelixe crate.
 
 The product is libhaelixe_cuda.so (C ABI: include/haelixe_cuda.h). This
-package holds its build recipe (build.py), the ctypes binding (_native.py)
-and a host-side mirror of haelixe's attention interface (attention.py).
+package holds its build recipe (build.py), the ctypes binding (_native.py),
+a host-side mirror of haelixe's attention interface (attention.py) and one of
+the attention layer's modules around it (nn.py: RMSNorm, Linear,
+MultiHeadAttention).
 """
 from .attention import (  # noqa: F401
     CudaAllocation,
@@ -17,3 +19,4 @@ from .attention import (  # noqa: F401
     rope_forward,
 )
 from ._native import HxError  # noqa: F401
+from . import nn  # noqa: F401

@@ -84,6 +84,10 @@ SIGNATURES = {
                                  _F, _I]),
     "hx_attn_bwd_rope_strided": (_I, [_P, _I, _SHP, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                       _U64, _F, _I, _F]),
+    "hx_linear_fwd": (_I, [_P, _I, _P, _P, _P, _P, _I, _I, _I]),
+    "hx_linear_bwd": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I]),
+    "hx_rmsnorm_fwd": (_I, [_P, _I, _P, _P, _P, _I, _I, _F]),
+    "hx_rmsnorm_bwd": (_I, [_P, _I, _P, _P, _P, _P, _P, _I, _I, _F]),
     "hx_rope_fwd": (_I, [_P, _I, _SHP, _P, _P, _F]),
     "hx_rope_bwd": (_I, [_P, _I, _SHP, _P, _P, _F]),
     "hx_reassemble_heads": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _I, _I]),

@@ -142,6 +142,19 @@ def _check_operands(*ts: torch.Tensor) -> None:
             raise ValueError("strided operands must share strides")
 
 
+def _like(t: torch.Tensor) -> torch.Tensor:
+    """An uninitialised tensor with exactly t's strides: every operand of one
+    call is addressed through the same [B, H, S, D] strides."""
+    return torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device=t.device)
+
+
+def _check_outputs(ref: torch.Tensor, *outs: Optional[torch.Tensor]) -> None:
+    for t in outs:
+        if t is not None and (t.shape != ref.shape or t.stride() != ref.stride() or t.dtype != ref.dtype
+                              or t.device != ref.device):
+            raise ValueError("output tensors must have the inputs' shape, strides, dtype and device")
+
+
 def _ptr(t: Optional[torch.Tensor]):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
@@ -152,8 +165,9 @@ def attn_forward(q, k, v, scale: float, causal: bool = False, out=None, lse=None
     ctx = context(q.device.index)
     ctx.use_stream()
     shp = _shape_of(q)
+    _check_outputs(q, out)
     if out is None:
-        out = torch.empty_like(q)
+        out = _like(q)
     if lse is None:
         lse = torch.empty(shp.B * shp.H * shp.S, device=q.device, dtype=torch.float32)
     N.check(N.lib().hx_attn_fwd_strided(ctx.handle, _DTYPES[q.dtype], ctypes.byref(shp),
@@ -170,14 +184,16 @@ def attn_backward(q, k, v, o, lse, dout, scale: float, causal: bool = False,
     dq, dk are returned with respect to the tensors before the rotation
     (rope_backward fused into the backward's last writes of dq and dk).
     """
-    dout = dout if dout.stride() == q.stride() else dout.contiguous()
+    if dout.stride() != q.stride():  # e.g. a contiguous upstream gradient of a strided view
+        dout = _like(q).copy_(dout)
     _check_operands(q, k, v, o, dout)
     ctx = context(q.device.index)
     ctx.use_stream()
     shp = _shape_of(q)
-    dq = torch.empty_like(q) if dq is None else dq
-    dk = torch.empty_like(q) if dk is None else dk
-    dv = torch.empty_like(q) if dv is None else dv
+    _check_outputs(q, dq, dk, dv)
+    dq = _like(q) if dq is None else dq
+    dk = _like(q) if dk is None else dk
+    dv = _like(q) if dv is None else dv
     if rope_base is None:
         N.check(N.lib().hx_attn_bwd_strided(ctx.handle, _DTYPES[q.dtype], ctypes.byref(shp),
                                             _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dout),
@@ -256,7 +272,8 @@ def rope_forward(x: torch.Tensor, base: float, out: Optional[torch.Tensor] = Non
     _check_operands(x)
     ctx = context(x.device.index)
     ctx.use_stream()
-    out = torch.empty_like(x) if out is None else out
+    _check_outputs(x, out)
+    out = _like(x) if out is None else out
     shp = _shape_of(x)
     N.check(N.lib().hx_rope_fwd(ctx.handle, _DTYPES[x.dtype], ctypes.byref(shp), _ptr(x),
                                 _ptr(out), float(base)), ctx.handle)
@@ -268,7 +285,8 @@ def rope_backward(g: torch.Tensor, base: float, out: Optional[torch.Tensor] = No
     _check_operands(g)
     ctx = context(g.device.index)
     ctx.use_stream()
-    out = torch.empty_like(g) if out is None else out
+    _check_outputs(g, out)
+    out = _like(g) if out is None else out
     shp = _shape_of(g)
     N.check(N.lib().hx_rope_bwd(ctx.handle, _DTYPES[g.dtype], ctypes.byref(shp), _ptr(g),
                                 _ptr(out), float(base)), ctx.handle)

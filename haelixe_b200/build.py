@@ -75,7 +75,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
                 if verbose or ptxas_info:
                     print(out)
     if force or jobs or _stale(LIB, objs):
-        cmd = [nvcc] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart"]
+        cmd = [nvcc] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart", "-lcublas"]
         run(cmd)
     return LIB
 

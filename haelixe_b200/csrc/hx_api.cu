@@ -8,6 +8,8 @@
 
 #include <algorithm>
 
+#include <cublas_v2.h>
+
 #include "hx_internal.h"
 
 namespace hx {
@@ -185,6 +187,7 @@ int hx_ctx_destroy(hx_ctx* c) {
     }
     for (auto& t : c->rope_tables) cudaFree(t.tab);
     c->rope_tables.clear();
+    if (c->blas) cublasDestroy((cublasHandle_t)c->blas);
     if (c->arena.pool) cudaMemPoolDestroy(c->arena.pool);
     if (c->status) cudaFree(c->status);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
@@ -594,6 +597,122 @@ int hx_reassemble_heads(hx_ctx* c, hx_dtype dt, const void* shards, void* out, i
 }
 
 uint64_t hx_kernel_launches(const hx_ctx* c) { return c ? c->kernel_launches : 0; }
+
+// ---- the attention block around the kernel: Linear and RMSNorm ------------
+
+static int blas_for(hx_ctx* c, cublasHandle_t* out) {
+    std::lock_guard<std::mutex> lk(c->blas_mu);
+    if (c->blas == nullptr) {
+        cublasHandle_t h;
+        if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS)
+            return set_error(c, HX_ERR_CUDA, "cublasCreate failed");
+        // Plain f32 (or bf16 in, f32 accumulate) arithmetic: no TF32 shortcuts.
+        cublasSetMathMode(h, CUBLAS_PEDANTIC_MATH);
+        c->blas = h;
+    }
+    *out = (cublasHandle_t)c->blas;
+    if (cublasSetStream(*out, c->stream) != CUBLAS_STATUS_SUCCESS)
+        return set_error(c, HX_ERR_CUDA, "cublasSetStream failed");
+    return HX_OK;
+}
+
+// Row-major C[m, n] = op(A) op(B) with A, B, C row-major, expressed as the
+// column-major product C^T = op(B)^T op(A)^T that cuBLAS computes.
+static int gemm_rm(hx_ctx* c, cublasHandle_t h, hx_dtype dt, bool ta, bool tb, int m, int n, int k,
+                   const void* A, int lda, const void* B, int ldb, void* C, int ldc, float beta,
+                   const char* who) {
+    const cudaDataType_t ty = dt == HX_BF16 ? CUDA_R_16BF : CUDA_R_32F;
+    const float alpha = 1.f;
+    const cublasStatus_t s = cublasGemmEx(h, tb ? CUBLAS_OP_T : CUBLAS_OP_N, ta ? CUBLAS_OP_T : CUBLAS_OP_N,
+                                          n, m, k, &alpha, B, ty, ldb, A, ty, lda, &beta, C, ty, ldc,
+                                          CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT);
+    if (s != CUBLAS_STATUS_SUCCESS) return set_error(c, HX_ERR_CUDA, "%s: cublasGemmEx status %d", who, (int)s);
+    return HX_OK;
+}
+
+static int linear_args(hx_ctx* c, hx_dtype dt, int rows, int in, int out, const char* who) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, who))) return st;
+    if (rows <= 0 || in <= 0 || out <= 0)
+        return set_error(c, HX_ERR_INVALID, "%s: rows, in_features, out_features must be positive", who);
+    return HX_OK;
+}
+
+int hx_linear_fwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w, const void* b, void* y, int rows,
+                  int in_features, int out_features) {
+    int st;
+    if ((st = linear_args(c, dt, rows, in_features, out_features, "hx_linear_fwd"))) return st;
+    if (!x || !w || !y) return set_error(c, HX_ERR_INVALID, "hx_linear_fwd: NULL operand");
+    DeviceGuard g(c->device);
+    LaunchCount lc(c);
+    cublasHandle_t h;
+    if ((st = blas_for(c, &h))) return st;
+    float beta = 0.f;
+    if (b != nullptr) {
+        if ((st = check_cuda(c, hx::bias_rows(c->stream, c->sm_count, dt, y, b, rows, out_features), "bias")))
+            return st;
+        beta = 1.f;
+    }
+    // y[rows, out] = x[rows, in] w[in, out] (+ the bias rows)
+    return gemm_rm(c, h, dt, false, false, rows, out_features, in_features, x, in_features, w, out_features, y,
+                   out_features, beta, "hx_linear_fwd");
+}
+
+int hx_linear_bwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w, const void* dy, void* dx, void* dw,
+                  void* db, int rows, int in_features, int out_features) {
+    int st;
+    if ((st = linear_args(c, dt, rows, in_features, out_features, "hx_linear_bwd"))) return st;
+    if (!dy || (dx && !w) || (dw && !x)) return set_error(c, HX_ERR_INVALID, "hx_linear_bwd: NULL operand");
+    DeviceGuard g(c->device);
+    LaunchCount lc(c);
+    cublasHandle_t h;
+    if ((st = blas_for(c, &h))) return st;
+    if (dx != nullptr &&  // dx[rows, in] = dy[rows, out] w[in, out]^T
+        (st = gemm_rm(c, h, dt, false, true, rows, in_features, out_features, dy, out_features, w, out_features,
+                      dx, in_features, 0.f, "hx_linear_bwd dx")))
+        return st;
+    if (dw != nullptr &&  // dw[in, out] = x[rows, in]^T dy[rows, out]
+        (st = gemm_rm(c, h, dt, true, false, in_features, out_features, rows, x, in_features, dy, out_features,
+                      dw, out_features, 0.f, "hx_linear_bwd dw")))
+        return st;
+    if (db != nullptr) {  // db[out] = sum over rows of dy
+        void* scratch = nullptr;
+        if ((st = hx_alloc(c, sizeof(float) * (uint64_t)out_features, &scratch))) return st;
+        st = check_cuda(c, hx::col_sum(c->stream, dt, dy, db, (float*)scratch, rows, out_features), "bias grad");
+        hx_free(c, scratch);
+    }
+    return st;
+}
+
+int hx_rmsnorm_fwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w, void* y, int rows, int hidden,
+                   float eps) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, "hx_rmsnorm_fwd"))) return st;
+    if (!x || !w || !y) return set_error(c, HX_ERR_INVALID, "hx_rmsnorm_fwd: NULL operand");
+    if (rows <= 0 || hidden <= 0 || !(eps >= 0.f))
+        return set_error(c, HX_ERR_INVALID, "hx_rmsnorm_fwd: rows, hidden must be positive, eps >= 0");
+    DeviceGuard g(c->device);
+    LaunchCount lc(c);
+    return check_cuda(c, hx::rmsnorm_fwd(c->stream, c->sm_count, dt, x, w, y, rows, hidden, eps), "hx_rmsnorm_fwd");
+}
+
+int hx_rmsnorm_bwd(hx_ctx* c, hx_dtype dt, const void* dy, const void* x, const void* w, void* dx, float* dw,
+                   int rows, int hidden, float eps) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, "hx_rmsnorm_bwd"))) return st;
+    if (!dy || !x || !w || !dx || !dw) return set_error(c, HX_ERR_INVALID, "hx_rmsnorm_bwd: NULL operand");
+    if (rows <= 0 || hidden <= 0 || !(eps >= 0.f))
+        return set_error(c, HX_ERR_INVALID, "hx_rmsnorm_bwd: rows, hidden must be positive, eps >= 0");
+    if (hidden > 16384)
+        return set_error(c, HX_ERR_UNSUPPORTED, "hx_rmsnorm_bwd: hidden %d > 16384 is not supported", hidden);
+    DeviceGuard g(c->device);
+    LaunchCount lc(c);
+    return check_cuda(c, hx::rmsnorm_bwd(c->stream, c->sm_count, dt, dy, x, w, dx, dw, rows, hidden, eps),
+                      "hx_rmsnorm_bwd");
+}
 
 int hx_last_path(const hx_ctx* c) { return c ? c->last_path : 0; }
 

@@ -53,6 +53,8 @@ struct hx_ctx {
     std::string last_error;
     std::mutex rope_mu;
     std::vector<hx::RopeTable> rope_tables;  // (cos, sin) tables, freed with the context
+    std::mutex blas_mu;
+    void* blas = nullptr;  // cublasHandle_t for the Linear GEMMs, created on first use
 };
 
 namespace hx {
@@ -91,6 +93,14 @@ cudaError_t sm100_attn_bwd(cudaStream_t st, int sm_count, DeviceStatus* status,
                            const void* o, const void* dout, const float* lse, void* dq,
                            void* dk, void* dv, void* workspace, float scale, int causal,
                            const float2* rope_tab = nullptr);
+
+// ---- the attention block around the kernel (mha_ops.cu) ----
+cudaError_t rmsnorm_fwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* x, const void* w, void* y,
+                        int rows, int hidden, float eps);
+cudaError_t rmsnorm_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* g, const void* x, const void* w,
+                        void* dx, float* dw, int rows, int hidden, float eps);
+cudaError_t bias_rows(cudaStream_t st, int sm_count, hx_dtype dt, void* y, const void* b, int64_t rows, int cols);
+cudaError_t col_sum(cudaStream_t st, hx_dtype dt, const void* dy, void* db, float* scratch, int64_t rows, int cols);
 
 // ---- head reassembly (heads.cu) ----
 cudaError_t reassemble_heads(cudaStream_t st, int elem_bytes, const void* src, void* dst, int n,

@@ -27,6 +27,10 @@
  *                                        (src/nn/attention.rs:62-73,91-94)
  *   hx_rope_fwd / hx_rope_bwd         <- rope_forward / rope_backward
  *                                        (src/kernels/rope.rs:5-82)
+ *   hx_linear_fwd / hx_linear_bwd     <- Linear::forward (src/nn/linear.rs:54-56)
+ *                                        and the matmul/add backward it records
+ *   hx_rmsnorm_fwd / hx_rmsnorm_bwd   <- rms_norm_forward / rms_norm_backward
+ *                                        (src/kernels/rms_norm.rs:20-132)
  *   hx_attn_bwd_rope_strided          <- FlashAttentionOp::backward followed by
  *                                        rope_backward of dq and dk (the rope ->
  *                                        attention order of src/nn/attention.rs:76-78)
@@ -193,6 +197,26 @@ int hx_rope_fwd(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape, const v
                 float base);
 int hx_rope_bwd(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape, const void* g, void* out,
                 float base);
+
+/* ---- the attention block around the kernel (src/nn/attention.rs:46-98) ------------ */
+/* y[rows, out] = x[rows, in] w[in, out] + b[out] (Linear::forward,
+ * src/nn/linear.rs:54-56, weight stored [in, out] as in linear.rs:41); b may be
+ * NULL. All row-major and contiguous. A cuBLAS GEMM with f32 accumulation and
+ * no TF32 (the reference multiplies in f32, src/kernels/matmul.rs). */
+int hx_linear_fwd(hx_ctx* ctx, hx_dtype dtype, const void* x, const void* w, const void* b, void* y,
+                  int rows, int in_features, int out_features);
+/* Its backward: dx = dy w^T, dw = x^T dy, db = column sums of dy; each of
+ * dx, dw, db may be NULL to skip it. */
+int hx_linear_bwd(hx_ctx* ctx, hx_dtype dtype, const void* x, const void* w, const void* dy, void* dx,
+                  void* dw, void* db, int rows, int in_features, int out_features);
+/* RMSNorm over the last dimension (src/kernels/rms_norm.rs:20-55):
+ * y = x / sqrt(mean(x^2) + eps) * w per row of `hidden` elements. */
+int hx_rmsnorm_fwd(hx_ctx* ctx, hx_dtype dtype, const void* x, const void* w, void* y, int rows,
+                   int hidden, float eps);
+/* Its backward (src/kernels/rms_norm.rs:57-132): dx, and dw in f32 summed
+ * over the rows. hidden <= 16384. */
+int hx_rmsnorm_bwd(hx_ctx* ctx, hx_dtype dtype, const void* dy, const void* x, const void* w, void* dx,
+                   float* dw, int rows, int hidden, float eps);
 
 /* ---- multi-GPU head sharding ------------------------------------------------------ */
 /* After an all-gather of per-rank head shards, shards holds n_shards

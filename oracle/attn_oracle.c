@@ -174,3 +174,47 @@ void ora_round_bf16(const float* x, float* y, long n) {
         memcpy(&y[i], &u, 4);
     }
 }
+
+/* Row-major out[m, n] = a[m, k] b[k, n]: the blocked i-p-j loop of
+ * src/kernels/matmul.rs:95-125 (Tensor::matmul on the CPU, used by
+ * Linear::forward, src/nn/linear.rs:55, and by its backward). */
+void ora_matmul(const float* a, const float* b, float* out, long m, long k, long n) {
+    matmul(a, b, out, m, k, n);
+}
+
+/* RMSNorm forward, src/kernels/rms_norm.rs:20-55: per row of `hidden`,
+ * sum_sq accumulated in order, inv_rms = 1 / sqrt(sum_sq / hidden + eps),
+ * out = x * inv_rms * w. */
+void ora_rms_norm_fwd(const float* x, const float* w, float* out, long rows, int hidden, float eps) {
+    for (long i = 0; i < rows; ++i) {
+        const float* xr = x + i * hidden;
+        float* yr = out + i * hidden;
+        float sum_sq = 0.0f;
+        for (int j = 0; j < hidden; ++j) sum_sq += xr[j] * xr[j];
+        const float inv_rms = 1.0f / sqrtf(sum_sq / (float)hidden + eps);
+        for (int j = 0; j < hidden; ++j) yr[j] = xr[j] * inv_rms * w[j];
+    }
+}
+
+/* RMSNorm backward, src/kernels/rms_norm.rs:57-132: inv_rms recomputed, then
+ * dot = sum g w x, dx = g w inv_rms - x inv_rms^3 dot / hidden and
+ * dw += g x inv_rms, summed over the rows in row order. */
+void ora_rms_norm_bwd(const float* g, const float* x, const float* w, float* dx, float* dw, long rows,
+                      int hidden, float eps) {
+    for (int j = 0; j < hidden; ++j) dw[j] = 0.0f;
+    for (long i = 0; i < rows; ++i) {
+        const float* gr = g + i * hidden;
+        const float* xr = x + i * hidden;
+        float* dxr = dx + i * hidden;
+        float sum_sq = 0.0f;
+        for (int j = 0; j < hidden; ++j) sum_sq += xr[j] * xr[j];
+        const float inv_rms = 1.0f / sqrtf(sum_sq / (float)hidden + eps);
+        float dot = 0.0f;
+        for (int j = 0; j < hidden; ++j) dot += gr[j] * w[j] * xr[j];
+        const float inv3 = inv_rms * inv_rms * inv_rms;
+        for (int j = 0; j < hidden; ++j) {
+            dxr[j] = (gr[j] * w[j] * inv_rms) - (xr[j] * inv3 * dot / (float)hidden);
+            dw[j] += gr[j] * xr[j] * inv_rms;
+        }
+    }
+}

@@ -45,6 +45,9 @@ def lib():
         L.ora_rope_fwd.argtypes = [_F, _F, l, i, i, f]
         L.ora_rope_bwd.argtypes = [_F, _F, l, i, i, f]
         L.ora_round_bf16.argtypes = [_F, _F, l]
+        L.ora_matmul.argtypes = [_F, _F, _F, l, l, l]
+        L.ora_rms_norm_fwd.argtypes = [_F, _F, _F, l, i, f]
+        L.ora_rms_norm_bwd.argtypes = [_F, _F, _F, _F, _F, l, i, f]
         L.ora_set_threads.argtypes = [i]
         L.ora_num_threads.restype = i
         _lib = L
@@ -131,3 +134,79 @@ def round_bf16(x) -> np.ndarray:
     y = np.empty_like(x)
     lib().ora_round_bf16(_p(x), _p(y), x.size)
     return y
+
+
+def matmul(a, b) -> np.ndarray:
+    """Row-major a[m, k] @ b[k, n] with the reference's blocked loop (kernels/matmul.rs)."""
+    a, b = _f32(a), _f32(b)
+    m, k = a.shape
+    k2, n = b.shape
+    assert k == k2
+    out = np.empty((m, n), np.float32)
+    lib().ora_matmul(_p(a), _p(b), _p(out), m, k, n)
+    return out
+
+
+def rms_norm_fwd(x, w, eps: float = 1e-5) -> np.ndarray:
+    """kernels/rms_norm.rs:20-55 over the last dimension."""
+    x, w = _f32(x), _f32(w)
+    out = np.empty_like(x)
+    lib().ora_rms_norm_fwd(_p(x), _p(w), _p(out), x.size // x.shape[-1], x.shape[-1], float(eps))
+    return out
+
+
+def rms_norm_bwd(g, x, w, eps: float = 1e-5):
+    """kernels/rms_norm.rs:57-132: (dx, dw)."""
+    g, x, w = _f32(g), _f32(x), _f32(w)
+    dx = np.empty_like(x)
+    dw = np.empty(x.shape[-1], np.float32)
+    lib().ora_rms_norm_bwd(_p(g), _p(x), _p(w), _p(dx), _p(dw), x.size // x.shape[-1], x.shape[-1],
+                           float(eps))
+    return dx, dw
+
+
+def mha_forward_backward(x, p: dict, dy, heads: int, rope_base: float = 10000.0, eps: float = 1e-5,
+                         causal: bool = False):
+    """MultiHeadAttention::forward (src/nn/attention.rs:46-98) on the CPU with
+    its backward through every op it records. x, dy: [B, S, hidden]; p holds
+    norm_w [hidden], wq/wk/wv/wo [hidden, hidden] (stored [in, out],
+    nn/linear.rs:41) and bq/bk/bv/bo [hidden]. Returns (y, grads) with grads
+    keyed dx, norm_w, wq, bq, ... as in p."""
+    x, dy = _f32(x), _f32(dy)
+    B, S, Hd = x.shape
+    H, D = heads, Hd // heads
+    scale = 1.0 / float(np.sqrt(np.float32(D)))
+    rows = B * S
+    x2 = x.reshape(rows, Hd)
+    n = rms_norm_fwd(x2, p["norm_w"], eps)                        # 1. pre-norm
+    proj = {c: matmul(n, p["w" + c]) + p["b" + c] for c in "qkv"}  # 2. Linear = matmul + add
+
+    def split(t):  # 3. [B, S, Hd] -> [B*H, S, D] (view, transpose(1, 2), view)
+        return np.ascontiguousarray(t.reshape(B, S, H, D).transpose(0, 2, 1, 3)).reshape(B * H, S, D)
+
+    def merge(t):  # 6. [B*H, S, D] -> [B, S, Hd]
+        return np.ascontiguousarray(t.reshape(B, H, S, D).transpose(0, 2, 1, 3)).reshape(rows, Hd)
+
+    q, k, v = (split(proj[c]) for c in "qkv")
+    qr, kr = rope_fwd(q, rope_base), rope_fwd(k, rope_base)        # 4. RoPE on Q and K
+    o, _ = attn_fwd(qr, kr, v, scale, causal)                      # 5. attention
+    om = merge(o)
+    y = matmul(om, p["wo"]) + p["bo"]                              # 7. out_proj
+    # backward, in reverse
+    g = {}
+    dy2 = dy.reshape(rows, Hd)
+    g["wo"] = matmul(np.ascontiguousarray(om.T), dy2)
+    g["bo"] = dy2.sum(axis=0, dtype=np.float32)
+    dom = matmul(dy2, np.ascontiguousarray(p["wo"].T))
+    do = split(dom.reshape(B, S, Hd))
+    dq, dk, dv = attn_bwd(qr, kr, v, do, scale, causal)
+    dq, dk = rope_bwd(dq, rope_base), rope_bwd(dk, rope_base)
+    dn = np.zeros((rows, Hd), np.float32)
+    for c, dt in zip("qkv", (dq, dk, dv)):
+        dproj = merge(dt)
+        g["w" + c] = matmul(np.ascontiguousarray(n.T), dproj)
+        g["b" + c] = dproj.sum(axis=0, dtype=np.float32)
+        dn += matmul(dproj, np.ascontiguousarray(p["w" + c].T))
+    g["dx"], g["norm_w"] = rms_norm_bwd(dn, x2, p["norm_w"], eps)
+    g["dx"] = g["dx"].reshape(B, S, Hd)
+    return y.reshape(B, S, Hd), g

@@ -1,0 +1,118 @@
+"""GPU parity of the attention block around the kernel (nn/attention.rs:46-98):
+RMSNorm, Linear and the whole MultiHeadAttention forward + backward, through the
+C ABI, against the CPU oracle (oracle.mha_forward_backward, itself checked
+against float64 autograd in test_oracle.py).
+
+Tolerances: max-abs 1e-3 for f32 (the C1 configuration: B2 S128 H4 D64, the
+reference's CPU-runnable layer). bf16 runs round every intermediate (norm output,
+projections, attention output) to bf16, so they are checked by relative L2
+error (2 %) against the oracle on the same bf16-rounded parameters and inputs.
+"""
+import numpy as np
+import pytest
+import torch
+
+import haelixe_b200 as hx
+from oracle import oracle as ora
+
+pytestmark = pytest.mark.gpu
+
+
+def _params(Hd, seed):
+    rng = np.random.default_rng(seed)
+    p = {"norm_w": rng.uniform(0.5, 1.5, Hd).astype(np.float32)}
+    for c in "qkvo":
+        p["w" + c] = (rng.uniform(-1, 1, (Hd, Hd)) * np.sqrt(6 / Hd)).astype(np.float32)
+        p["b" + c] = rng.uniform(-0.1, 0.1, Hd).astype(np.float32)
+    return p
+
+
+def _module(Hd, H, p, dtype, causal=False):
+    m = hx.nn.MultiHeadAttention(Hd, H, device="cuda", dtype=dtype, causal=causal)
+    with torch.no_grad():
+        m.norm.weight.copy_(torch.from_numpy(p["norm_w"]))
+        for c, lin in zip("qkvo", (m.q_proj, m.k_proj, m.v_proj, m.out_proj)):
+            lin.weight.copy_(torch.from_numpy(p["w" + c]))
+            lin.bias.copy_(torch.from_numpy(p["b" + c]))
+    return m
+
+
+def _grads(m):
+    g = {"norm_w": m.norm.weight.grad}
+    for c, lin in zip("qkvo", (m.q_proj, m.k_proj, m.v_proj, m.out_proj)):
+        g["w" + c], g["b" + c] = lin.weight.grad, lin.bias.grad
+    return {k: v.float().cpu().numpy() for k, v in g.items()}
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+def test_rmsnorm_and_linear_match_oracle(dtype):
+    rng = np.random.default_rng(3)
+    rows, fin, fout = 37, 96, 80
+    rnd = (lambda a: ora.round_bf16(a)) if dtype == torch.bfloat16 else (lambda a: a)
+    x = rnd(rng.standard_normal((rows, fin), dtype=np.float32))
+    w = rnd(rng.standard_normal((fin, fout), dtype=np.float32) * 0.1)
+    b = rnd(rng.standard_normal(fout, dtype=np.float32))
+    nw = rnd(rng.uniform(0.5, 1.5, fin).astype(np.float32))
+    g = rnd(rng.standard_normal((rows, fout), dtype=np.float32))
+    gn = rnd(rng.standard_normal((rows, fin), dtype=np.float32))
+    dev = lambda a: torch.from_numpy(a).to(dtype).cuda().requires_grad_()
+    xt, wt, bt, nwt = dev(x), dev(w), dev(b), dev(nw)
+    y = hx.nn.linear(xt, wt, bt)
+    y.backward(torch.from_numpy(g).to(dtype).cuda())
+    n = hx.nn.rms_norm(xt.detach().requires_grad_(), nwt)
+    xn = n
+    n.backward(torch.from_numpy(gn).to(dtype).cuda())
+    ry = ora.matmul(x, w) + b
+    rdx = ora.matmul(g, np.ascontiguousarray(w.T))
+    rdw = ora.matmul(np.ascontiguousarray(x.T), g)
+    rn = ora.rms_norm_fwd(x, nw)
+    rndx, rndw = ora.rms_norm_bwd(gn, x, nw)
+    tol = 1e-3 if dtype == torch.float32 else 5e-2
+    for name, got, ref in (("y", y, ry), ("dx", xt.grad, rdx), ("dw", wt.grad, rdw),
+                           ("db", bt.grad, g.sum(0)), ("norm", xn, rn), ("dw_norm", nwt.grad, rndw)):
+        got = got.detach().float().cpu().numpy()
+        err = np.abs(got - ref).max() / max(1.0, np.abs(ref).max())
+        assert err < tol, (name, err)
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+def test_mha_c1_matches_oracle(causal):
+    """C1: B2 S128 hidden 256 (H4 D64), f32, RoPE base 10000."""
+    B, S, H, D = 2, 128, 4, 64
+    Hd = H * D
+    p = _params(Hd, 21)
+    rng = np.random.default_rng(22)
+    x = rng.standard_normal((B, S, Hd), dtype=np.float32)
+    dy = rng.standard_normal((B, S, Hd), dtype=np.float32)
+    m = _module(Hd, H, p, torch.float32, causal)
+    xt = torch.from_numpy(x).cuda().requires_grad_()
+    y = m(xt)
+    y.backward(torch.from_numpy(dy).cuda())
+    ry, rg = ora.mha_forward_backward(x, p, dy, H, rope_base=10000.0, causal=causal)
+    got = _grads(m)
+    got["dx"] = xt.grad.cpu().numpy()
+    assert np.abs(y.detach().cpu().numpy() - ry).max() < 1e-3
+    for k in rg:
+        err = np.abs(got[k] - rg[k]).max()
+        assert err < 1e-3, (k, err)
+
+
+def test_mha_bf16_uses_tcgen05_and_matches_oracle():
+    B, S, H, D = 2, 256, 4, 128
+    Hd = H * D
+    p = {k: ora.round_bf16(v) for k, v in _params(Hd, 31).items()}
+    rng = np.random.default_rng(32)
+    x = ora.round_bf16(rng.standard_normal((B, S, Hd), dtype=np.float32))
+    dy = ora.round_bf16(rng.standard_normal((B, S, Hd), dtype=np.float32))
+    m = _module(Hd, H, p, torch.bfloat16, causal=True)
+    xt = torch.from_numpy(x).to(torch.bfloat16).cuda().requires_grad_()
+    y = m(xt)
+    assert hx.context().last_path == "tcgen05"
+    y.backward(torch.from_numpy(dy).to(torch.bfloat16).cuda())
+    ry, rg = ora.mha_forward_backward(x, p, dy, H, rope_base=10000.0, causal=True)
+    got = _grads(m)
+    got["dx"] = xt.grad.float().cpu().numpy()
+    got["y"], rg["y"] = y.detach().float().cpu().numpy(), ry
+    for k in rg:
+        rel = np.linalg.norm(got[k] - rg[k]) / max(np.linalg.norm(rg[k]), 1e-6)
+        assert rel < 2e-2, (k, rel)

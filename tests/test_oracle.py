@@ -188,3 +188,66 @@ def test_bf16_rounding_is_round_to_nearest_even():
     mine = ora.round_bf16(x)
     ref = torch.tensor(x).to(torch.bfloat16).to(torch.float32).numpy()
     np.testing.assert_array_equal(mine, ref)
+
+
+# ---- the attention block around the kernel (nn/attention.rs, kernels/rms_norm.rs) ----
+
+def _torch_rope(x, base):
+    """Interleaved-pair rotation by s * base^(-2i/D), in float64 (kernels/rope.rs:23-40)."""
+    S, D = x.shape[-2], x.shape[-1]
+    i = torch.arange(D // 2, dtype=torch.float64)
+    freq = base ** (-(2 * i) / D)
+    th = torch.arange(S, dtype=torch.float64)[:, None] * freq[None, :]
+    c, s = torch.cos(th), torch.sin(th)
+    x0, x1 = x[..., 0::2], x[..., 1::2]
+    return torch.stack((x0 * c - x1 * s, x0 * s + x1 * c), dim=-1).reshape(x.shape)
+
+
+def test_rms_norm_matches_autograd():
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((7, 48), dtype=np.float32)
+    w = rng.standard_normal(48, dtype=np.float32)
+    g = rng.standard_normal((7, 48), dtype=np.float32)
+    xt, wt = (torch.tensor(a, dtype=torch.float64, requires_grad=True) for a in (x, w))
+    yt = xt / torch.sqrt((xt * xt).mean(-1, keepdim=True) + 1e-5) * wt
+    yt.backward(torch.tensor(g, dtype=torch.float64))
+    y = ora.rms_norm_fwd(x, w)
+    dx, dw = ora.rms_norm_bwd(g, x, w)
+    assert np.abs(y - yt.detach().numpy()).max() < 1e-5
+    assert np.abs(dx - xt.grad.numpy()).max() < 1e-4
+    assert np.abs(dw - wt.grad.numpy()).max() < 1e-4
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_mha_composition_matches_autograd(causal):
+    """oracle.mha_forward_backward against a float64 autograd model of
+    MultiHeadAttention::forward (nn/attention.rs:46-98)."""
+    B, S, H, D = 2, 12, 2, 8
+    Hd = H * D
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((B, S, Hd), dtype=np.float32)
+    dy = rng.standard_normal((B, S, Hd), dtype=np.float32)
+    p = {"norm_w": rng.uniform(0.5, 1.5, Hd).astype(np.float32)}
+    for c in "qkvo":
+        p["w" + c] = (rng.uniform(-1, 1, (Hd, Hd)) * np.sqrt(6 / Hd)).astype(np.float32)
+        p["b" + c] = rng.uniform(-0.1, 0.1, Hd).astype(np.float32)
+    y, g = ora.mha_forward_backward(x, p, dy, H, rope_base=10000.0, causal=causal)
+    pt = {k: torch.tensor(v, dtype=torch.float64, requires_grad=True) for k, v in p.items()}
+    xt = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    n = xt / torch.sqrt((xt * xt).mean(-1, keepdim=True) + 1e-5) * pt["norm_w"]
+
+    def split(t):
+        return t.reshape(B, S, H, D).transpose(1, 2)
+
+    q, k, v = (split(n @ pt["w" + c] + pt["b" + c]) for c in "qkv")
+    q, k = _torch_rope(q, 10000.0), _torch_rope(k, 10000.0)
+    s = (q @ k.transpose(-1, -2)) / np.sqrt(D)
+    if causal:
+        s = s.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool), 1), float("-inf"))
+    o = torch.softmax(s, -1) @ v
+    yt = o.transpose(1, 2).reshape(B, S, Hd) @ pt["wo"] + pt["bo"]
+    yt.backward(torch.tensor(dy, dtype=torch.float64))
+    assert np.abs(y - yt.detach().numpy()).max() < 1e-4
+    assert np.abs(g["dx"] - xt.grad.numpy()).max() < 1e-4
+    for key in p:
+        assert np.abs(g[key] - pt[key].grad.numpy()).max() < 2e-4, key
