@@ -73,6 +73,7 @@ struct Bars {
     uint64_t q_full;
     uint64_t k_full[STAGES], k_empty[STAGES], v_full[STAGES], v_empty[STAGES];
     uint64_t s_full[NWG], p_full[NWG], o_full[NWG];
+    uint64_t p_half[NWG];  // P of the tile's first 64 keys is in TMEM
     uint64_t turn[NWG];  // ping-pong token between the softmax warpgroups
     uint64_t done;
     uint32_t tmem_base;
@@ -88,6 +89,8 @@ struct FwdParams {
     int causal;
     DeviceStatus* status;
 };
+
+static_assert(sizeof(Bars<4>) <= 256, "barrier block");
 
 __device__ __forceinline__ uint32_t bar_addr(const uint64_t& b) { return smem_addr(&b); }
 
@@ -129,6 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int w = 0; w < NWG; ++w) {
             mbar_init(bar_addr(bars->s_full[w]), 1);
             mbar_init(bar_addr(bars->p_full[w]), BM);
+            mbar_init(bar_addr(bars->p_half[w]), BM);
             mbar_init(bar_addr(bars->o_full[w]), 1);
             mbar_init(bar_addr(bars->turn[w]), BM);
         }
@@ -225,15 +229,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     umma_ss(dS, desc_of(dq + kmaj(kk), hi), desc_of(dk + kmaj(kk), hi), idS, kk > 0);
                 umma_commit(bar_addr(bars->s_full[w]));
             };
-            auto issue_PV = [&](int w, int st, int j) {
+            // O_w += P_w V_j over the K steps of keys [half*64, half*64+64).
+            auto issue_PV = [&](int w, int st, int j, int half) {
                 const uint32_t dO = tmem + (w ? C::O_COL1 : C::O_COL0);
                 const uint32_t aP = tmem + (w ? C::S_COL1 : C::S_COL0);
                 const uint32_t dv = lV + st * kTile;
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; ++kk)
+                for (int kk = half * (BN / 32); kk < (half + 1) * (BN / 32); ++kk)
                     umma_ts(dO, aP + kk * 8, desc_of(dv + kk * (2048 >> 4), hi), idO,
                             (j > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(bar_addr(bars->o_full[w]));
+                if (half) umma_commit(bar_addr(bars->o_full[w]));
             };
             bool ok = mbar_wait(bar_addr(bars->q_full), 0, abort_flag, p.status, 20);
             if (ok && n_kv > 0) {
@@ -255,10 +260,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bool k_next = false;
                 for (int w = 0; w < NWG && ok; ++w) {
                     if (j < n_w[w]) {
+                        // The first half of PV runs while the warpgroup is still
+                        // exponentiating the tile's last 64 keys.
+                        if (!(ok = mbar_wait(bar_addr(bars->p_half[w]), j & 1, abort_flag, p.status, 25)))
+                            break;
+                        tc_fence_after();
+                        issue_PV(w, st, j, 0);
                         if (!(ok = mbar_wait(bar_addr(bars->p_full[w]), j & 1, abort_flag, p.status, 23)))
                             break;
                         tc_fence_after();
-                        issue_PV(w, st, j);
+                        issue_PV(w, st, j, 1);
                     }
                     if (jn < n_w[w]) {
                         if (!k_next) {
@@ -342,6 +353,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 rescale = true;
             }
             l_run *= alpha;
+            // O is rescaled before any of P(j) is published (PV(j) accumulates
+            // onto it). It already holds all of PV(j-1): the MMA thread issued
+            // PV(j-1) before S(j), and S(j) has completed.
+            if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+                for (int c = 0; c < D; c += 32) {
+                    uint32_t o[32];
+                    tmem_ld32(tO + c, o);
+                    tmem_ld_wait();
+                    reg_fence<32>(o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(tO + c, o);
+                }
+            }
             // x = s * scale * log2(e) - m and the row sum run two columns per
             // instruction (f32x2); the exponentials stay on the MUFU.
             const uint64_t sl2x2 = f2_pack(p.sl2, p.sl2);
@@ -365,29 +391,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     pk[i] = pack_bf16(p0, p1);
                 }
                 tmem_st16(tS + c / 2, pk);
+                if (c == BN / 2 - 32) {  // keys [0, 64) done: publish the first half of P
+                    tmem_st_wait();
+                    tc_fence_before();
+                    mbar_arrive(bar_addr(bars->p_half[w]));
+                }
             }
             float s0, s1;
             f2_unpack(f2_add(sum_a, sum_b), s0, s1);
             const float sum = s0 + s1;
             mbar_arrive(bar_addr(bars->turn[w ^ 1]));  // the partner's turn
-            // O is rescaled after P is written (the scores are dead by then)
-            // and before P is published: PV(j) cannot start earlier, and
-            // PV(j-1) of this tile must have landed.
-            if (__any_sync(0xffffffffu, rescale)) {
-                if (!(ok = mbar_wait(bar_addr(bars->o_full[w]), (j - 1) & 1, abort_flag, p.status, 31)))
-                    break;
-                tc_fence_after();
-#pragma unroll
-                for (int c = 0; c < D; c += 32) {
-                    uint32_t o[32];
-                    tmem_ld32(tO + c, o);
-                    tmem_ld_wait();
-                    reg_fence<32>(o);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(tO + c, o);
-                }
-            }
             l_run += sum;
             m_run = m_use;
             tmem_st_wait();
