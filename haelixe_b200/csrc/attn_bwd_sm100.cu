@@ -85,6 +85,10 @@ struct BCfg {
     // TMEM columns. D=128: two S^T buffers (the next tile's K Q^T runs while P of
     // this one is computed) and one dQ^T buffer; D=64: one S^T buffer, two dQ.
     static constexpr int NSB = D == 128 ? 2 : 1;
+    // D=128: dS^T is also packed into the S^T buffer's free half, after P^T,
+    // and dK reads it from TMEM (TS UMMA) instead of from the smem tile; the
+    // buffer is released after dK. D=64 (one S^T buffer) keeps dK on smem.
+    static constexpr bool DK_TS = NSB == 2;
     static constexpr int NDQ = D == 128 ? 1 : 2;
     static constexpr int DQ_COLS = DQ_T ? BQ : D;
     static constexpr uint32_t C_S0 = 0, C_DP = NSB * BQ, C_DQ0 = C_DP + BQ,
@@ -348,15 +352,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kk = 0; kk < NA; ++kk)  // dV += P^T dO
                     umma_ts(tmem + C::C_DV, tmem + cS + acc_a(kk), dDOm + mnmaj(kk), idAcc,
                             (first && kk == 0) ? 0u : 1u);
-                umma_commit(bar_addr(bars->sfree[b]));
+                if (!C::DK_TS) umma_commit(bar_addr(bars->sfree[b]));
                 if (!(ok = mbar_wait(bar_addr(bars->ds_full[it & 1]), (it >> 1) & 1, abort_flag, p.status,
                                      54)))
                     break;
                 tc_fence_after();
+                if constexpr (C::DK_TS) {
 #pragma unroll
-                for (int kk = 0; kk < NA; ++kk)  // dK += dS^T Q (dS^T K-major from smem)
-                    umma_ss(tmem + C::C_DK, dsk + kmaj(kk, C::CHUNK_DS), dQm + mnmaj(kk), idAcc,
-                            (first && kk == 0) ? 0u : 1u);
+                    for (int kk = 0; kk < NA; ++kk)  // dK += dS^T Q (dS^T from TMEM, after P^T)
+                        umma_ts(tmem + C::C_DK, tmem + cS + acc_a(kk) + BQ / 4, dQm + mnmaj(kk), idAcc,
+                                (first && kk == 0) ? 0u : 1u);
+                    umma_commit(bar_addr(bars->sfree[b]));
+                } else {
+#pragma unroll
+                    for (int kk = 0; kk < NA; ++kk)  // dK += dS^T Q (dS^T K-major from smem)
+                        umma_ss(tmem + C::C_DK, dsk + kmaj(kk, C::CHUNK_DS), dQm + mnmaj(kk), idAcc,
+                                (first && kk == 0) ? 0u : 1u);
+                }
                 // Q(it) and dO(it) are read by nothing after dK(it): S^T(it) and
                 // dP^T(it) completed before dS(it) existed.
                 umma_commit(bar_addr(bars->q_empty[st]));
@@ -485,7 +497,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<uint4*>(ds_row + chunk * C::CHUNK_DS + ((u ^ (r & 7)) * 16)) =
                     make_uint4(pk[4 * u8], pk[4 * u8 + 1], pk[4 * u8 + 2], pk[4 * u8 + 3]);
             }
+            if constexpr (C::DK_TS) {  // packed dS^T after this warpgroup's P^T columns
+#pragma unroll
+                for (int c = 0; c < HC / 2; c += 16) tmem_st16(tl + cS + HC / 2 + c, pk + c);
+                tmem_st_wait();
+            }
             fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
+            tc_fence_before();
             mbar_arrive(bar_addr(bars->ds_full[it & 1]));
         }
         // Epilogue: warpgroup 0 stores dV, warpgroup 1 stores dK (times scale).
