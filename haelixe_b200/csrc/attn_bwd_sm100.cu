@@ -629,7 +629,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Per row (b, h, s) of the padded [B*H][S_pad] tables: lse2 = lse * log2(e)
 // and delta = rowsum(dO * O) in f32 (0 for s >= S), and zero the row of the
-// dQ accumulator. One warp per row.
+// dQ accumulator. D/8 lanes per row, 16-byte loads, 32/(D/8) rows per warp,
+// grid-stride over row groups.
 template <int D>
 __global__ void __launch_bounds__(256) bwd_pre_kernel(const __nv_bfloat16* __restrict__ o,
                                                       const __nv_bfloat16* __restrict__ dout,
@@ -638,47 +639,44 @@ __global__ void __launch_bounds__(256) bwd_pre_kernel(const __nv_bfloat16* __res
                                                       float* __restrict__ delta,
                                                       float* __restrict__ dq_acc, AttnDims d,
                                                       int S_pad) {
+    constexpr int G = D / 8;     // lanes per row
+    constexpr int RPW = 32 / G;  // rows per warp
     const int64_t rows = (int64_t)d.B * d.H * S_pad;
-    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
-    const int lane = threadIdx.x % 32;
-    if (r >= rows) return;
-    const int s = (int)(r % S_pad);
-    const int64_t bhi = r / S_pad;
-    if (s >= d.S) {
-        if (lane == 0) {
-            lse2[r] = 0.f;
-            delta[r] = 0.f;
-        }
-        return;
-    }
-    const int hi = (int)(bhi % d.H), bi = (int)(bhi / d.H);
-    const int64_t off = (int64_t)bi * d.sb + (int64_t)hi * d.sh + (int64_t)s * d.ss;
-    constexpr int PER = D / 32;  // elements per lane (2 or 4)
-    float acc = 0.f;
-    if (PER == 4) {
-        const uint2 a = *reinterpret_cast<const uint2*>(o + off + lane * 4);
-        const uint2 g = *reinterpret_cast<const uint2*>(dout + off + lane * 4);
-        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
+    const int lane = threadIdx.x % 32, sub = lane % G;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x / 32);
+    for (int64_t r0 = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * RPW; r0 < rows;
+         r0 += nwarps * RPW) {
+        const int64_t r = r0 + lane / G;
+        const bool row_ok = r < rows;
+        const int s = row_ok ? (int)(r % S_pad) : 0;
+        const int64_t bhi = row_ok ? r / S_pad : 0;
+        const bool in_seq = row_ok && s < d.S;
+        float acc = 0.f;
+        if (in_seq) {
+            const int hi = (int)(bhi % d.H), bi = (int)(bhi / d.H);
+            const int64_t off = (int64_t)bi * d.sb + (int64_t)hi * d.sh + (int64_t)s * d.ss + sub * 8;
+            const uint4 a = *reinterpret_cast<const uint4*>(o + off);
+            const uint4 g = *reinterpret_cast<const uint4*>(dout + off);
+            const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+            const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const float2 x = __bfloat1622float2(a2[i]), y = __bfloat1622float2(g2[i]);
-            acc += x.x * y.x + x.y * y.y;
+            for (int i = 0; i < 4; ++i) {
+                const float2 x = __bfloat1622float2(a2[i]), y = __bfloat1622float2(g2[i]);
+                acc += x.x * y.x + x.y * y.y;
+            }
         }
-    } else {
-        const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(o + off + lane * 2);
-        const __nv_bfloat162 g = *reinterpret_cast<const __nv_bfloat162*>(dout + off + lane * 2);
-        const float2 x = __bfloat1622float2(a), y = __bfloat1622float2(g);
-        acc = x.x * y.x + x.y * y.y;
-    }
 #pragma unroll
-    for (int w = 16; w > 0; w >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, w);
-    if (lane == 0) {
-        delta[r] = acc;
-        lse2[r] = lse[bhi * d.S + s] * kLog2e;
+        for (int w = G / 2; w > 0; w >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, w);
+        if (row_ok && sub == 0) {
+            delta[r] = in_seq ? acc : 0.f;
+            lse2[r] = in_seq ? lse[bhi * d.S + s] * kLog2e : 0.f;
+        }
+        if (in_seq) {
+            float4* z = reinterpret_cast<float4*>(dq_acc + (bhi * d.S + s) * D) + sub * 2;
+            z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+            z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     }
-    float4* z = reinterpret_cast<float4*>(dq_acc + (bhi * d.S + s) * D);
-    for (int i = lane; i < D / 4; i += 32) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // dQ = bf16(scale * accumulator); 8 elements per thread.
@@ -745,7 +743,9 @@ cudaError_t launch(cudaStream_t st, int sm_count, DeviceStatus* status, const At
     using C = BCfg<D>;
     const BwdWorkspace w = carve(ws, d);
     const int64_t rows_pad = (int64_t)d.B * d.H * w.S_pad;
-    bwd_pre_kernel<D><<<(unsigned)((rows_pad * 32 + 255) / 256), 256, 0, st>>>(
+    int64_t pre_blocks = (rows_pad / (32 / (D / 8)) + 7) / 8;  // 8 warps per block
+    if (pre_blocks > (int64_t)sm_count * 16) pre_blocks = (int64_t)sm_count * 16;
+    bwd_pre_kernel<D><<<(unsigned)pre_blocks, 256, 0, st>>>(
         (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, lse, w.lse2, w.delta, w.dq_acc, d,
         w.S_pad);
     note_launch();
