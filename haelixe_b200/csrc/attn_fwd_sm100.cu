@@ -17,9 +17,13 @@
 //               lane l of warp w owns query row 32*(w%4)+l of its tile (the
 //               TMEM lane quadrant warp w may access), so row
 //               max and row sum need no shuffles. P is written back over S
-//               as packed bf16. O is rescaled in TMEM only when the running
-//               max grows by more than 2^8 (the stale max is exact after the
-//               final division by l, which uses the same max).
+//               as packed bf16, published in two halves (keys 0-63, then
+//               64-127) so the first half of PV runs while the second half is
+//               still being exponentiated. O is rescaled in TMEM, before any
+//               of P(j) is published, only when the running max grows by more
+//               than 2^8 (the stale max is exact after the final division by
+//               l, which uses the same max). The two warpgroups take turns on
+//               the exponentials (ping-pong mbarriers).
 // The MMA order S0(j+1) right after PV0(j) lets softmax of one tile overlap
 // the tensor core work of the other.
 //
