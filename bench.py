@@ -199,7 +199,7 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.sm), "source": self.source}
 
 
-def cpu_baseline(q, k, v, do, scale, causal, budget_s=12.0, max_slices=4):
+def cpu_baseline(q, k, v, do, scale, causal, budget_s=12.0, max_slices=32):
     """Oracle (C restatement of the reference's CPU path) on whole (b,h) slices."""
     from oracle import oracle as ora
     B, H, S, D = q.shape
