@@ -116,3 +116,30 @@ def test_mha_bf16_uses_tcgen05_and_matches_oracle():
     for k in rg:
         rel = np.linalg.norm(got[k] - rg[k]) / max(np.linalg.norm(rg[k]), 1e-6)
         assert rel < 2e-2, (k, rel)
+
+
+def test_mha_c1_exact_configuration():
+    """The reference's CPU-runnable case as specified: f32, batch 2, seq 128,
+    d_model 256, 4 heads x 64, causal; x and Wq/Wk/Wv/Wo i.i.d. N(0, 0.02),
+    biases 0, RMSNorm weight 1; loss = sum of outputs (upstream gradient ones);
+    outputs and all gradients within 1e-3."""
+    B, S, H, D = 2, 128, 4, 64
+    Hd = H * D
+    rng = np.random.default_rng(2024)
+    p = {"norm_w": np.ones(Hd, np.float32)}
+    for c in "qkvo":
+        p["w" + c] = (rng.standard_normal((Hd, Hd)) * 0.02).astype(np.float32)
+        p["b" + c] = np.zeros(Hd, np.float32)
+    x = (rng.standard_normal((B, S, Hd)) * 0.02).astype(np.float32)
+    dy = np.ones((B, S, Hd), np.float32)
+    m = _module(Hd, H, p, torch.float32, causal=True)
+    xt = torch.from_numpy(x).cuda().requires_grad_()
+    y = m(xt)
+    y.sum().backward()
+    ry, rg = ora.mha_forward_backward(x, p, dy, H, rope_base=10000.0, causal=True)
+    got = _grads(m)
+    got["dx"] = xt.grad.cpu().numpy()
+    assert np.abs(y.detach().cpu().numpy() - ry).max() < 1e-3
+    for k in rg:
+        err = np.abs(got[k] - rg[k]).max()
+        assert err < 1e-3, (k, err)
