@@ -115,14 +115,6 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
 }
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int c0, int c1) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
-        : "memory");
-}
 
 // Plain bulk copy global -> this CTA's smem (16-byte aligned, size % 16 == 0).
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
@@ -145,10 +137,6 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, uint32
 __device__ __forceinline__ void bulk_commit_group() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
-// Waits until the smem sources of this thread's committed bulk groups were read.
-__device__ __forceinline__ void bulk_wait_group_read0() {
-    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
 // Waits until at most N of this thread's committed bulk groups still have to
 // read their smem sources.
 template <int N>
@@ -158,10 +146,6 @@ __device__ __forceinline__ void bulk_wait_group_read() {
 // Waits until this thread's committed bulk groups completed.
 __device__ __forceinline__ void bulk_wait_group0() {
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-}
-// Barrier among `count` threads (a multiple of 32) on hardware barrier `id` (1..15).
-__device__ __forceinline__ void named_barrier(int id, int count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // ---- tcgen05: TMEM allocation ---------------------------------------------------
@@ -230,13 +214,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
         "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
         "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
         : HX_R8(0), HX_R8(8), HX_R8(16), HX_R8(24)
-        : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-        : HX_R8(0), HX_R8(8)
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
@@ -312,11 +289,6 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
     uint64_t r;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
 // max of three floats in one instruction (sm_100).
