@@ -385,9 +385,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t x = f2_fma(
                         f2_pack(__uint_as_float(s[c + 2 * i]), __uint_as_float(s[c + 2 * i + 1])),
                         sl2x2, negx2);
-                    float x0, x1;
-                    f2_unpack(x, x0, x1);
-                    const float p0 = ex2(x0), p1 = ex2(x1);
+                    // D=64 has half the MMA work per tile and is bound by the
+                    // multi-function unit: one pair in four goes to the FMA pipe.
+                    float p0, p1;
+                    if (D == 64 && (i & 3) == 3) {
+                        f2_unpack(ex2_poly_x2(x), p0, p1);
+                    } else {
+                        float x0, x1;
+                        f2_unpack(x, x0, x1);
+                        p0 = ex2(x0);
+                        p1 = ex2(x1);
+                    }
                     if (i & 1)
                         sum_b = f2_add(sum_b, f2_pack(p0, p1));
                     else
