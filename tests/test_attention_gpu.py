@@ -298,3 +298,16 @@ def test_standalone_op_b8_h16_s2048_d64_causal():
 
 def test_llama_layer_b4_h32_s8192_d128_causal_rope():
     _sampled_full_size(4, 32, 8192, 128, True, rope_base=500000.0, samples=((3, 31),))
+
+
+def test_full_mask_long_sequences():
+    """Non-causal at full length on the tcgen05 path, both head dims (every key
+    tile of every query tile, no masked tiles skipped)."""
+    _sampled_full_size(1, 4, 8192, 128, False, samples=((0, 3),))
+    _sampled_full_size(2, 4, 4096, 64, False, samples=((1, 0),))
+
+
+def test_ragged_lengths_tcgen05():
+    """Sequence lengths that leave partial K/V and query tiles at the end."""
+    for S, D in ((1000, 128), (2049, 64), (1537, 128)):
+        _sampled_full_size(1, 2, S, D, True, samples=((0, 1),))
