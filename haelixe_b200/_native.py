@@ -94,6 +94,7 @@ SIGNATURES = {
     "hx_kernel_launches": (_U64, [_P]),
     "hx_last_path": (_I, [_P]),
     "hx_set_force_simt": (_I, [_P, _I]),
+    "hx_selftest_wait_timeout": (_I, [_P]),
 }
 
 

@@ -716,6 +716,13 @@ int hx_rmsnorm_bwd(hx_ctx* c, hx_dtype dt, const void* dy, const void* x, const 
 
 int hx_last_path(const hx_ctx* c) { return c ? c->last_path : 0; }
 
+int hx_selftest_wait_timeout(hx_ctx* c) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    DeviceGuard g(c->device);
+    LaunchCount lc(c);
+    return check_cuda(c, hx::selftest_wait_timeout(c->stream, c->status), "hx_selftest_wait_timeout");
+}
+
 int hx_set_force_simt(hx_ctx* c, int force) {
     if (c == nullptr) return HX_ERR_INVALID;
     c->force_simt = force ? 1 : 0;

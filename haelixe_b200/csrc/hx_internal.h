@@ -102,6 +102,9 @@ cudaError_t rmsnorm_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* 
 cudaError_t bias_rows(cudaStream_t st, int sm_count, hx_dtype dt, void* y, const void* b, int64_t rows, int cols);
 cudaError_t col_sum(cudaStream_t st, hx_dtype dt, const void* dy, void* db, float* scratch, int64_t rows, int cols);
 
+// ---- failure-path self-test (selftest.cu) ----
+cudaError_t selftest_wait_timeout(cudaStream_t st, DeviceStatus* status);
+
 // ---- head reassembly (heads.cu) ----
 cudaError_t reassemble_heads(cudaStream_t st, int elem_bytes, const void* src, void* dst, int n,
                              int B, int Hs, int S, int D, int layout, int sm_count);

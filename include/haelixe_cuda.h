@@ -234,6 +234,11 @@ uint64_t hx_kernel_launches(const hx_ctx* ctx);
 int hx_last_path(const hx_ctx* ctx);
 /* Forces the SIMT kernels (1) or restores automatic selection (0). */
 int hx_set_force_simt(hx_ctx* ctx, int force);
+/* Exercises the kernels' failure path: enqueues one CTA whose bounded
+ * mbarrier wait can never complete. After the wait limit (2 s) it records the
+ * expiry in the context's status word and exits normally (no trap, no hang),
+ * so the next hx_sync returns HX_ERR_TIMEOUT and later calls work as usual. */
+int hx_selftest_wait_timeout(hx_ctx* ctx);
 
 #ifdef __cplusplus
 }

@@ -99,3 +99,44 @@ def test_head_range_partitions_heads():
         assert all(a[1] == b[0] for a, b in zip(got, got[1:]))
     with pytest.raises(ValueError):
         head_range(0, 3, 32)
+
+
+def _leaving_worker(rank, world, port, q):
+    """Rank 1 raises before the output all-gather; rank 0 must get an error, not hang."""
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    try:
+        h0, h1 = head_range(rank, world, H)
+        o_shard = torch.zeros(B, h1 - h0, S, D)
+        if rank == 1:
+            raise RuntimeError("rank 1 fails between steps")
+        parts = [torch.empty_like(o_shard) for _ in range(world)]
+        try:
+            dist.all_gather(parts, o_shard)
+            q.put((rank, "gathered"))
+        except Exception as e:  # the peer left: the collective reports it
+            q.put((rank, "error: " + type(e).__name__))
+    except RuntimeError:
+        q.put((rank, "raised"))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_rank_failure_surfaces_as_an_error_on_the_other_rank():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert got[1] == "raised"
+    assert got[0].startswith("error"), got[0]
