@@ -95,6 +95,7 @@ SIGNATURES = {
     "hx_last_path": (_I, [_P]),
     "hx_set_force_simt": (_I, [_P, _I]),
     "hx_selftest_wait_timeout": (_I, [_P]),
+    "hx_arena_set_limit": (_I, [_P, _U64]),
 }
 
 

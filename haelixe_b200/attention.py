@@ -84,6 +84,10 @@ class CudaContext:
         N.check(N.lib().hx_arena_stats_get(self.handle, ctypes.byref(s)), self.handle)
         return {f: int(getattr(s, f)) for f, _ in N.ArenaStats._fields_}
 
+    def set_arena_limit(self, nbytes: int) -> None:
+        """Caps the arena's held bytes (0 removes the cap): past it allocations fail with OOM."""
+        N.check(N.lib().hx_arena_set_limit(self.handle, int(nbytes)), self.handle)
+
     def arena_reset(self) -> None:
         N.check(N.lib().hx_arena_reset(self.handle), self.handle)
 

@@ -270,6 +270,20 @@ int hx_alloc(hx_ctx* c, uint64_t bytes, void** ptr) {
     }
     // Miss: the mutex is released before the driver call (arena.rs:45-47).
     DeviceGuard g(c->device);
+    uint64_t limit, held;
+    {
+        std::lock_guard<std::mutex> lk(c->arena.mu);
+        limit = c->arena.limit;
+        held = c->arena.live_bytes + c->arena.cached_bytes;
+    }
+    if (limit != 0 && held + bin > limit) {
+        hx_arena_reset(c);  // parked slabs count against the budget: give them back first
+        std::lock_guard<std::mutex> lk(c->arena.mu);
+        if (c->arena.live_bytes + bin > limit)
+            return set_error(c, HX_ERR_OOM, "hx_alloc: %llu bytes (bin) over the arena limit of %llu (%llu live)",
+                             (unsigned long long)bin, (unsigned long long)limit,
+                             (unsigned long long)c->arena.live_bytes);
+    }
     void* p = nullptr;
     cudaError_t e = cudaMallocFromPoolAsync(&p, bin, c->arena.pool, c->stream);
     if (e == cudaErrorMemoryAllocation) {
@@ -313,6 +327,13 @@ int hx_arena_reset(hx_ctx* c) {
     c->arena.free_list.clear();
     c->arena.cached_bytes = 0;
     return check_cuda(c, cudaGetLastError(), "cudaFreeAsync");
+}
+
+int hx_arena_set_limit(hx_ctx* c, uint64_t bytes) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(c->arena.mu);
+    c->arena.limit = bytes;
+    return HX_OK;
 }
 
 int hx_arena_stats_get(const hx_ctx* c, hx_arena_stats* out) {

@@ -35,6 +35,7 @@ struct Arena {
     std::unordered_map<uint64_t, std::vector<void*>> free_list;  // bin -> slabs
     std::unordered_map<void*, uint64_t> live;                    // slab -> bin
     uint64_t live_bytes = 0, cached_bytes = 0, hits = 0, misses = 0;
+    uint64_t limit = 0;  // bytes the arena may hold (live + parked); 0 = no limit
 };
 
 }  // namespace hx

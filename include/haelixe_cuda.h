@@ -119,6 +119,11 @@ int hx_alloc(hx_ctx* ctx, uint64_t bytes, void** ptr);
 int hx_free(hx_ctx* ctx, void* ptr);
 /* Releases every parked slab back to the CUDA pool (arena.rs:76-80). */
 int hx_arena_reset(hx_ctx* ctx);
+/* Caps the bytes the arena may hold (handed out plus parked; 0 = no cap, the
+ * reference's behaviour). An allocation past the cap first releases the
+ * parked slabs, then fails with HX_ERR_OOM instead of growing the pool: a
+ * memory budget for callers that share the GPU, and a way to test exhaustion. */
+int hx_arena_set_limit(hx_ctx* ctx, uint64_t bytes);
 int hx_arena_stats_get(const hx_ctx* ctx, hx_arena_stats* out);
 
 /* ---- transfers --------------------------------------------------------------- */

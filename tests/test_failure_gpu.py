@@ -105,3 +105,29 @@ def test_mha_ops_write_only_their_outputs():
                    (gdb, rows * fin), (gwb, fin)):
         assert _bands_intact(buf, n)
     assert torch.allclose(y, x @ w + b, atol=1e-4, rtol=1e-4)
+
+
+def test_arena_limit_reports_oom_and_recovers():
+    """Allocator exhaustion simulated with a capped arena: the call fails with
+    HX_ERR_OOM (HxError in Python) instead of growing the pool, and works again
+    once the cap is lifted."""
+    import ctypes
+    ctx = hx.context()
+    lib = N.lib()
+    q, k, v, do = (torch.randn(1, 2, 4096, 128, device="cuda").to(torch.bfloat16) for _ in range(4))
+    o, lse = hx.attn_forward(q, k, v, 0.088, True)
+    torch.cuda.synchronize()
+    ctx.arena_reset()
+    ctx.set_arena_limit(1 << 20)
+    try:
+        p = ctypes.c_void_p()
+        assert lib.hx_alloc(ctx.handle, 2 << 20, ctypes.byref(p)) == N.HX_ERR_OOM
+        assert "arena limit" in N.last_error(ctx.handle)
+        with pytest.raises(N.HxError) as e:  # the backward's workspace (> 4 MB) comes from the arena
+            hx.attn_backward(q, k, v, o, lse, do, 0.088, True)
+        assert e.value.status == N.HX_ERR_OOM
+    finally:
+        ctx.set_arena_limit(0)
+    dq, dk, dv = hx.attn_backward(q, k, v, o, lse, do, 0.088, True)
+    ctx.sync()
+    assert torch.isfinite(dq.float()).all()
