@@ -9,6 +9,7 @@
 #include <algorithm>
 
 #include <cublas_v2.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include "hx_internal.h"
 
@@ -43,6 +44,13 @@ using hx::check_cuda;
 using hx::set_error;
 
 namespace {
+
+// An NVTX range named after the public call, so that profiler timelines
+// (nsys, ncu's NVTX filters) show the library's calls around their kernels.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+};
 
 // Adds the kernels launched during one public call to the context's count.
 struct LaunchCount {
@@ -400,6 +408,7 @@ int hx_attn_fwd_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, cons
     if (!q || !k || !v || !o) return set_error(c, HX_ERR_INVALID, "hx_attn_fwd: NULL operand");
     if (!isfinite(scale)) return set_error(c, HX_ERR_INVALID, "hx_attn_fwd: scale is not finite");
     DeviceGuard g(c->device);
+    NvtxRange nv("hx_attn_fwd_strided");
     LaunchCount lc(c);
     const hx::AttnDims d = hx::dims_of(*shape);
     const bool fast = !c->force_simt && lse != nullptr && hx::sm100_supported(dt, d) &&
@@ -467,6 +476,7 @@ static int attn_bwd_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, c
         return set_error(c, HX_ERR_INVALID, "hx_attn_bwd: NULL operand");
     if (!isfinite(scale)) return set_error(c, HX_ERR_INVALID, "hx_attn_bwd: scale is not finite");
     DeviceGuard g(c->device);
+    NvtxRange nv(rope_base ? "hx_attn_bwd_rope" : "hx_attn_bwd");
     LaunchCount lc(c);
     if (rope_base != nullptr && (st = rope_table_for(c, shape, *rope_base, &tab, "hx_attn_bwd_rope")))
         return st;
@@ -584,6 +594,7 @@ static int rope_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const
     if (!isfinite(base) || base <= 0.f)
         return set_error(c, HX_ERR_INVALID, "%s: base must be positive and finite", who);
     DeviceGuard g(c->device);
+    NvtxRange nv(who);
     LaunchCount lc(c);
     float2* tab = nullptr;
     if ((st = rope_table_for(c, shape, base, &tab, who))) return st;
@@ -610,6 +621,7 @@ int hx_reassemble_heads(hx_ctx* c, hx_dtype dt, const void* shards, void* out, i
         (out_layout != 0 && out_layout != 1))
         return set_error(c, HX_ERR_INVALID, "hx_reassemble_heads: bad arguments");
     DeviceGuard g(c->device);
+    NvtxRange nv("hx_reassemble_heads");
     LaunchCount lc(c);
     return check_cuda(c, hx::reassemble_heads(c->stream, dt == HX_F32 ? 4 : 2, shards, out,
                                               n_shards, B, H_shard, S, D, out_layout,
@@ -666,6 +678,7 @@ int hx_linear_fwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w, const vo
     if ((st = linear_args(c, dt, rows, in_features, out_features, "hx_linear_fwd"))) return st;
     if (!x || !w || !y) return set_error(c, HX_ERR_INVALID, "hx_linear_fwd: NULL operand");
     DeviceGuard g(c->device);
+    NvtxRange nv("hx_linear_fwd");
     LaunchCount lc(c);
     cublasHandle_t h;
     if ((st = blas_for(c, &h))) return st;
@@ -686,6 +699,7 @@ int hx_linear_bwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w, const vo
     if ((st = linear_args(c, dt, rows, in_features, out_features, "hx_linear_bwd"))) return st;
     if (!dy || (dx && !w) || (dw && !x)) return set_error(c, HX_ERR_INVALID, "hx_linear_bwd: NULL operand");
     DeviceGuard g(c->device);
+    NvtxRange nv("hx_linear_bwd");
     LaunchCount lc(c);
     cublasHandle_t h;
     if ((st = blas_for(c, &h))) return st;
@@ -715,6 +729,7 @@ int hx_rmsnorm_fwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w, void* y
     if (rows <= 0 || hidden <= 0 || !(eps >= 0.f))
         return set_error(c, HX_ERR_INVALID, "hx_rmsnorm_fwd: rows, hidden must be positive, eps >= 0");
     DeviceGuard g(c->device);
+    NvtxRange nv("hx_rmsnorm_fwd");
     LaunchCount lc(c);
     return check_cuda(c, hx::rmsnorm_fwd(c->stream, c->sm_count, dt, x, w, y, rows, hidden, eps), "hx_rmsnorm_fwd");
 }
@@ -730,6 +745,7 @@ int hx_rmsnorm_bwd(hx_ctx* c, hx_dtype dt, const void* dy, const void* x, const 
     if (hidden > 16384)
         return set_error(c, HX_ERR_UNSUPPORTED, "hx_rmsnorm_bwd: hidden %d > 16384 is not supported", hidden);
     DeviceGuard g(c->device);
+    NvtxRange nv("hx_rmsnorm_bwd");
     LaunchCount lc(c);
     return check_cuda(c, hx::rmsnorm_bwd(c->stream, c->sm_count, dt, dy, x, w, dx, dw, rows, hidden, eps),
                       "hx_rmsnorm_bwd");
@@ -740,6 +756,7 @@ int hx_last_path(const hx_ctx* c) { return c ? c->last_path : 0; }
 int hx_selftest_wait_timeout(hx_ctx* c) {
     if (c == nullptr) return HX_ERR_INVALID;
     DeviceGuard g(c->device);
+    NvtxRange nv("hx_selftest_wait_timeout");
     LaunchCount lc(c);
     return check_cuda(c, hx::selftest_wait_timeout(c->stream, c->status), "hx_selftest_wait_timeout");
 }
