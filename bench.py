@@ -11,6 +11,12 @@ Metric: attention fwd+bwd TFLOP/s, FlashAttention convention
 (fwd 4*B*H*S^2*D, bwd 2.5x fwd, causal halves both: 7*B*H*S^2*D), whole job.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl haelixe|reference]
+
+`--workload block_stack` instead times a context workload, not the headline:
+one training step of an 8-block TransformerBlock language model (d_model
+2048, 16 heads x 128, GELU MLP 8192, final RMSNorm, vocab 32000, batch 2 x
+seq 4096, causal, bf16 storage with f32 master weights, AdamW), every op
+through the library (attention kernels, cuBLAS GEMMs, element kernels).
 """
 from __future__ import annotations
 
@@ -66,6 +72,7 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=6)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", choices=["attention", "block_stack"], default="attention")
     return p.parse_args()
 
 
@@ -500,8 +507,85 @@ def e2e_measure(a, ctx, N, torch, dev, world, sets, step, total_flops):
             "h2d_bytes_per_step": int(bi), "d2h_bytes_per_step": int(bo)}
 
 
+def run_block_stack(a):
+    """The block-stack training step (context workload, 1 GPU; under torchrun
+    only rank 0 runs it)."""
+    import torch
+
+    import haelixe_b200 as hx
+    from haelixe_b200 import _native as N
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, S, Hd, H, L, V = 2, 4096, 2048, 16, 8, 32000
+    model = hx.nn.BlockStack(V, Hd, H, L, device=dev, dtype=torch.bfloat16, rope_base=10000.0, causal=True,
+                             init_std=0.02, seed=a.seed)
+    params = model.parameters()
+    opt = hx.optim.AdamW(1e-4)
+    ctx = hx.context(local)
+    g = torch.Generator().manual_seed(a.seed)
+    ids_h = torch.randint(0, V, (B, S), generator=g, dtype=torch.int32).pin_memory()
+    tgt_h = torch.randint(0, V, (B * S,), generator=g, dtype=torch.int32).pin_memory()
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+    ids = torch.empty_like(ids_h, device=dev)
+    tgt = torch.empty_like(tgt_h, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        ids.copy_(ids_h, non_blocking=True)
+        tgt.copy_(tgt_h, non_blocking=True)
+        loss = model.loss(ids, tgt)
+        loss.backward()
+        opt.step([(q, q.grad) for q in params])
+        for q in params:
+            q.grad = None
+        loss_h.copy_(loss, non_blocking=True)
+
+    losses = []
+    for _ in range(a.warmup):
+        step()
+        torch.cuda.synchronize()
+        losses.append(float(loss_h.item()))
+    sampler = ClockSampler(local)
+    sampler.start()
+    launches0 = N.lib().hx_kernel_launches(ctx.handle)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for _ in range(a.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = t0.elapsed_time(t1) / a.steps
+    n_lin = sum(q.numel() for q in params if q.dim() == 2 and q is not model.embed.weight)
+    flops = 6.0 * n_lin * B * S + L * attn_flops(B, H, S, Hd // H, True)
+    tok_s = B * S / (ms * 1e-3)
+    print(json.dumps({
+        "metric": "block-stack training step tokens/s (context workload)", "value": tok_s, "unit": "tokens/s",
+        "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform token ids, N(0,0.02) init)",
+        "config": {"workload": f"{L}-block TransformerBlock LM d{Hd} H{H}x{Hd // H} MLP {4 * Hd} vocab {V} "
+                               f"B{B} S{S} causal, bf16 + f32 master, AdamW",
+                   "parameters": int(sum(q.numel() for q in params)),
+                   "l2": "activations and weights far larger than L2"},
+        "model_tflops": flops / (ms * 1e-3) / 1e12, "flops_per_step": flops,
+        "loss_warmup": losses, "loss": float(loss_h.item()),
+        "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": int(ids_h.numel() * 4 + tgt_h.numel() * 4),
+                "d2h_bytes_per_step": 4, "note": "token ids in and the loss out every step, inside the timed region"},
+        "gpu_launches": int(N.lib().hx_kernel_launches(ctx.handle) - launches0),
+        "clocks": clocks,
+    }), flush=True)
+    return 0
+
+
 def main():
     a = parse()
+    if a.workload == "block_stack":
+        return run_block_stack(a)
     if a.impl == "reference":
         return run_reference(a)
     return run_haelixe(a)

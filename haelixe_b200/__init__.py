@@ -2,9 +2,10 @@
 
 The product is libhaelixe_cuda.so (C ABI: include/haelixe_cuda.h). This
 package holds its build recipe (build.py), the ctypes binding (_native.py),
-a host-side mirror of haelixe's attention interface (attention.py) and one of
-the attention layer's modules around it (nn.py: RMSNorm, Linear,
-MultiHeadAttention).
+a host-side mirror of haelixe's attention interface (attention.py), the
+modules around it (nn.py: RMSNorm, Linear, MultiHeadAttention, FeedForward,
+TransformerBlock, Embedding, cross_entropy, BlockStack) and the optimizer
+(optim.py: AdamW).
 """
 from .attention import (  # noqa: F401
     CudaAllocation,
@@ -19,4 +20,4 @@ from .attention import (  # noqa: F401
     rope_forward,
 )
 from ._native import HxError  # noqa: F401
-from . import nn  # noqa: F401
+from . import nn, optim  # noqa: F401

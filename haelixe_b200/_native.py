@@ -44,6 +44,13 @@ class ArenaStats(ctypes.Structure):
 _lib = None
 
 _P = ctypes.c_void_p
+class AdamWTensor(ctypes.Structure):
+    """hx_adamw_tensor."""
+    _fields_ = [("param", ctypes.c_void_p), ("grad", ctypes.c_void_p), ("m", ctypes.c_void_p),
+                ("v", ctypes.c_void_p), ("param_lowp", ctypes.c_void_p), ("n", ctypes.c_uint64),
+                ("grad_dtype", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
 _I = ctypes.c_int
 _U64 = ctypes.c_uint64
 _F = ctypes.c_float
@@ -88,6 +95,13 @@ SIGNATURES = {
     "hx_linear_bwd": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I]),
     "hx_rmsnorm_fwd": (_I, [_P, _I, _P, _P, _P, _I, _I, _F]),
     "hx_rmsnorm_bwd": (_I, [_P, _I, _P, _P, _P, _P, _P, _I, _I, _F]),
+    "hx_linear_residual_fwd": (_I, [_P, _I, _P, _P, _P, _P, _P, _I, _I, _I]),
+    "hx_cross_entropy": (_I, [_P, _I, _P, _P, _P, _P, _I, _I]),
+    "hx_adamw_step": (_I, [_P, _P, _I, _F, _F, _F, _F, _F, _I]),
+    "hx_embedding_fwd": (_I, [_P, _I, _P, _P, _P, _U64, _I, _I]),
+    "hx_embedding_bwd": (_I, [_P, _I, _P, _P, _P, _U64, _I, _I]),
+    "hx_gelu_fwd": (_I, [_P, _I, _P, _P, _U64]),
+    "hx_gelu_bwd": (_I, [_P, _I, _P, _P, _P, _U64]),
     "hx_rope_fwd": (_I, [_P, _I, _SHP, _P, _P, _F]),
     "hx_rope_bwd": (_I, [_P, _I, _SHP, _P, _P, _F]),
     "hx_reassemble_heads": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _I, _I]),

@@ -639,8 +639,10 @@ static int blas_for(hx_ctx* c, cublasHandle_t* out) {
         cublasHandle_t h;
         if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS)
             return set_error(c, HX_ERR_CUDA, "cublasCreate failed");
-        // Plain f32 (or bf16 in, f32 accumulate) arithmetic: no TF32 shortcuts.
-        cublasSetMathMode(h, CUBLAS_PEDANTIC_MATH);
+        // Default math: bf16 operands run on the tensor cores with f32
+        // accumulation; f32 operands stay f32 (TF32 is used only when asked
+        // for with CUBLAS_COMPUTE_32F_FAST_TF32 or CUBLAS_TF32_TENSOR_OP_MATH).
+        cublasSetMathMode(h, CUBLAS_DEFAULT_MATH);
         c->blas = h;
     }
     *out = (cublasHandle_t)c->blas;
@@ -658,7 +660,7 @@ static int gemm_rm(hx_ctx* c, cublasHandle_t h, hx_dtype dt, bool ta, bool tb, i
     const float alpha = 1.f;
     const cublasStatus_t s = cublasGemmEx(h, tb ? CUBLAS_OP_T : CUBLAS_OP_N, ta ? CUBLAS_OP_T : CUBLAS_OP_N,
                                           n, m, k, &alpha, B, ty, ldb, A, ty, lda, &beta, C, ty, ldc,
-                                          CUBLAS_COMPUTE_32F_PEDANTIC, CUBLAS_GEMM_DEFAULT);
+                                          CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
     if (s != CUBLAS_STATUS_SUCCESS) return set_error(c, HX_ERR_CUDA, "%s: cublasGemmEx status %d", who, (int)s);
     return HX_OK;
 }
@@ -749,6 +751,144 @@ int hx_rmsnorm_bwd(hx_ctx* c, hx_dtype dt, const void* dy, const void* x, const 
     LaunchCount lc(c);
     return check_cuda(c, hx::rmsnorm_bwd(c->stream, c->sm_count, dt, dy, x, w, dx, dw, rows, hidden, eps),
                       "hx_rmsnorm_bwd");
+}
+
+int hx_gelu_fwd(hx_ctx* c, hx_dtype dt, const void* x, void* y, uint64_t n) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, "hx_gelu_fwd"))) return st;
+    if (!x || !y) return set_error(c, HX_ERR_INVALID, "hx_gelu_fwd: NULL operand");
+    if (n == 0) return HX_OK;
+    DeviceGuard g(c->device);
+    NvtxRange nv("hx_gelu_fwd");
+    LaunchCount lc(c);
+    return check_cuda(c, hx::gelu_fwd(c->stream, c->sm_count, dt, x, y, (int64_t)n), "hx_gelu_fwd");
+}
+
+int hx_gelu_bwd(hx_ctx* c, hx_dtype dt, const void* dy, const void* x, void* dx, uint64_t n) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, "hx_gelu_bwd"))) return st;
+    if (!dy || !x || !dx) return set_error(c, HX_ERR_INVALID, "hx_gelu_bwd: NULL operand");
+    if (n == 0) return HX_OK;
+    DeviceGuard g(c->device);
+    NvtxRange nv("hx_gelu_bwd");
+    LaunchCount lc(c);
+    return check_cuda(c, hx::gelu_bwd(c->stream, c->sm_count, dt, dy, x, dx, (int64_t)n), "hx_gelu_bwd");
+}
+
+// ---- the training step around the block stack ------------------------------
+
+int hx_linear_residual_fwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w, const void* b,
+                           const void* residual, void* y, int rows, int in_features, int out_features) {
+    int st;
+    if ((st = linear_args(c, dt, rows, in_features, out_features, "hx_linear_residual_fwd"))) return st;
+    if (!x || !w || !y) return set_error(c, HX_ERR_INVALID, "hx_linear_residual_fwd: NULL operand");
+    DeviceGuard g(c->device);
+    NvtxRange nv("hx_linear_residual_fwd");
+    LaunchCount lc(c);
+    cublasHandle_t h;
+    if ((st = blas_for(c, &h))) return st;
+    float beta = 0.f;
+    if (b != nullptr || residual != nullptr) {
+        if ((st = check_cuda(c, hx::residual_bias(c->stream, c->sm_count, dt, y, residual, b, rows, out_features),
+                             "residual rows")))
+            return st;
+        beta = 1.f;
+    }
+    return gemm_rm(c, h, dt, false, false, rows, out_features, in_features, x, in_features, w, out_features, y,
+                   out_features, beta, "hx_linear_residual_fwd");
+}
+
+int hx_cross_entropy(hx_ctx* c, hx_dtype dt, const void* logits, const uint32_t* targets, float* loss,
+                     void* dlogits, int rows, int classes) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, "hx_cross_entropy"))) return st;
+    if (!logits || !targets || !loss) return set_error(c, HX_ERR_INVALID, "hx_cross_entropy: NULL operand");
+    if (rows <= 0 || classes <= 0)
+        return set_error(c, HX_ERR_INVALID, "hx_cross_entropy: rows and classes must be positive");
+    DeviceGuard g(c->device);
+    NvtxRange nv("hx_cross_entropy");
+    LaunchCount lc(c);
+    void* row_loss = nullptr;
+    if ((st = hx_alloc(c, sizeof(float) * (uint64_t)rows, &row_loss))) return st;
+    st = check_cuda(c, hx::cross_entropy(c->stream, dt, logits, targets, (float*)row_loss, loss, dlogits, rows,
+                                         classes),
+                    "hx_cross_entropy");
+    hx_free(c, row_loss);
+    return st;
+}
+
+// f32 a^n by binary exponentiation with one rounding per product: the
+// evaluation of Rust's f32::powi for a run-time exponent (the llvm.powi
+// intrinsic's square-and-multiply routine). n >= 0 here.
+static float powi_f32(float a, int n) {
+    float r = 1.0f;
+    for (;;) {
+        if (n & 1) r *= a;
+        n /= 2;
+        if (n == 0) break;
+        a *= a;
+    }
+    return r;
+}
+
+int hx_adamw_step(hx_ctx* c, const hx_adamw_tensor* tensors, int count, float lr, float beta1, float beta2,
+                  float eps, float weight_decay, int step) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    if (count < 0 || (count > 0 && tensors == nullptr) || step < 1)
+        return set_error(c, HX_ERR_INVALID, "hx_adamw_step: bad tensor list or step < 1");
+    for (int i = 0; i < count; ++i) {
+        const hx_adamw_tensor& t = tensors[i];
+        if (t.n == 0) continue;
+        if (!t.param || !t.grad || !t.m || !t.v || (t.grad_dtype != HX_F32 && t.grad_dtype != HX_BF16))
+            return set_error(c, HX_ERR_INVALID, "hx_adamw_step: tensor %d has a NULL pointer or bad dtype", i);
+    }
+    if (count == 0) return HX_OK;
+    DeviceGuard g(c->device);
+    NvtxRange nv("hx_adamw_step");
+    LaunchCount lc(c);
+    const float bc1 = 1.0f - powi_f32(beta1, step);
+    const float bc2 = 1.0f - powi_f32(beta2, step);
+    return check_cuda(c, hx::adamw_step(c->stream, c->sm_count, tensors, count, lr, beta1, beta2, eps,
+                                        weight_decay, bc1, bc2),
+                      "hx_adamw_step");
+}
+
+static int embedding_args(hx_ctx* c, hx_dtype dt, const void* a, const uint32_t* ids, const void* b, int vocab,
+                          int dim, const char* who) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, who))) return st;
+    if (!a || !ids || !b) return set_error(c, HX_ERR_INVALID, "%s: NULL operand", who);
+    if (vocab <= 0 || dim <= 0) return set_error(c, HX_ERR_INVALID, "%s: vocab and dim must be positive", who);
+    return HX_OK;
+}
+
+int hx_embedding_fwd(hx_ctx* c, hx_dtype dt, const void* table, const uint32_t* ids, void* out, uint64_t tokens,
+                     int vocab, int dim) {
+    int st;
+    if ((st = embedding_args(c, dt, table, ids, out, vocab, dim, "hx_embedding_fwd"))) return st;
+    if (tokens == 0) return HX_OK;
+    DeviceGuard g(c->device);
+    NvtxRange nv("hx_embedding_fwd");
+    LaunchCount lc(c);
+    return check_cuda(c, hx::embedding_fwd(c->stream, c->sm_count, dt, table, ids, out, (int64_t)tokens, vocab, dim),
+                      "hx_embedding_fwd");
+}
+
+int hx_embedding_bwd(hx_ctx* c, hx_dtype dt, const void* dout, const uint32_t* ids, float* dtable, uint64_t tokens,
+                     int vocab, int dim) {
+    int st;
+    if ((st = embedding_args(c, dt, dout, ids, dtable, vocab, dim, "hx_embedding_bwd"))) return st;
+    if (tokens == 0) return HX_OK;
+    DeviceGuard g(c->device);
+    NvtxRange nv("hx_embedding_bwd");
+    LaunchCount lc(c);
+    return check_cuda(c, hx::embedding_bwd(c->stream, c->sm_count, dt, dout, ids, dtable, (int64_t)tokens, vocab,
+                                           dim),
+                      "hx_embedding_bwd");
 }
 
 int hx_last_path(const hx_ctx* c) { return c ? c->last_path : 0; }

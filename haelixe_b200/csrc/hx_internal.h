@@ -101,6 +101,18 @@ cudaError_t rmsnorm_fwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* 
 cudaError_t rmsnorm_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* g, const void* x, const void* w,
                         void* dx, float* dw, int rows, int hidden, float eps);
 cudaError_t bias_rows(cudaStream_t st, int sm_count, hx_dtype dt, void* y, const void* b, int64_t rows, int cols);
+cudaError_t cross_entropy(cudaStream_t st, hx_dtype dt, const void* logits, const uint32_t* targets,
+                          float* row_loss, float* loss, void* dlogits, int rows, int classes);
+cudaError_t adamw_step(cudaStream_t st, int sm_count, const hx_adamw_tensor* tensors, int count, float lr,
+                       float beta1, float beta2, float eps, float weight_decay, float bc1, float bc2);
+cudaError_t embedding_fwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* table, const uint32_t* ids,
+                          void* out, int64_t tokens, int vocab, int dim);
+cudaError_t embedding_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* dout, const uint32_t* ids,
+                          float* dtable, int64_t tokens, int vocab, int dim);
+cudaError_t residual_bias(cudaStream_t st, int sm_count, hx_dtype dt, void* y, const void* res, const void* b,
+                          int64_t rows, int cols);
+cudaError_t gelu_fwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* x, void* y, int64_t n);
+cudaError_t gelu_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* g, const void* x, void* dx, int64_t n);
 cudaError_t col_sum(cudaStream_t st, hx_dtype dt, const void* dy, void* db, float* scratch, int64_t rows, int cols);
 
 // ---- failure-path self-test (selftest.cu) ----

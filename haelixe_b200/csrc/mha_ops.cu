@@ -1,8 +1,10 @@
-// Device kernels of the attention block around the fused attention
-// (MultiHeadAttention::forward, src/nn/attention.rs:46-98): RMSNorm forward
-// and backward (src/kernels/rms_norm.rs:20-132) and the bias broadcast /
-// column-sum kernels of Linear (src/nn/linear.rs:54-56). The Linear GEMMs
-// themselves are plain cuBLAS calls (hx_api.cu).
+// Device kernels of the layers around the fused attention
+// (MultiHeadAttention::forward, src/nn/attention.rs:46-98, and the
+// TransformerBlock's FeedForward, src/nn/mlp.rs): RMSNorm forward and
+// backward (src/kernels/rms_norm.rs:20-132), GELU forward and backward
+// (src/kernels/activations.rs:192-237) and the bias broadcast / column-sum
+// kernels of Linear (src/nn/linear.rs:54-56). The Linear GEMMs themselves are
+// plain cuBLAS calls (hx_api.cu).
 //
 // RMSNorm: one warp per row, f32 statistics. The forward keeps the
 // reference's expression order: inv_rms = 1 / sqrt(sum_sq / hidden + eps),
@@ -121,6 +123,33 @@ __global__ void __launch_bounds__(256) store_f32_kernel(const float* __restrict_
     if (i < n) st(out, i, a[i]);
 }
 
+// GELU, tanh form (activations.rs:200-206): c = sqrt(2/pi),
+// y = 0.5 x (1 + tanh(c (x + 0.044715 x^3))).
+template <typename T>
+__global__ void __launch_bounds__(256) gelu_fwd_kernel(const T* x, T* y, int64_t n) {  // x, y may alias
+    const float c = 0.7978845608028654f;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = ld(x, i);
+        const float t = tanhf(c * (v + 0.044715f * (v * v * v)));
+        st(y, i, 0.5f * v * (1.0f + t));
+    }
+}
+
+// Its exact derivative (activations.rs:222-234):
+// dx = g (0.5 (1 + t) + 0.5 x (1 - t^2) c (1 + 3 * 0.044715 x^2)).
+template <typename T>
+__global__ void __launch_bounds__(256) gelu_bwd_kernel(const T* __restrict__ g, const T* __restrict__ x,
+                                                       T* __restrict__ dx, int64_t n) {
+    const float c = 0.7978845608028654f;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = ld(x, i);
+        const float t = tanhf(c * (v + 0.044715f * (v * v * v)));
+        const float sech2 = 1.0f - t * t;
+        const float d_inner = c * (1.0f + 3.0f * 0.044715f * (v * v));
+        st(dx, i, ld(g, i) * (0.5f * (1.0f + t) + 0.5f * v * sech2 * d_inner));
+    }
+}
+
 int grid_for(int64_t work, int per_block, int sm_count) {
     int64_t b = (work + per_block - 1) / per_block;
     const int64_t cap = (int64_t)sm_count * 8;
@@ -161,6 +190,27 @@ cudaError_t rmsnorm_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* 
         rmsnorm_bwd_kernel<float><<<grid, 256, smem, st>>>((const float*)g, (const float*)x, (const float*)w,
                                                            (float*)dx, dw, rows, hidden, eps);
     }
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t gelu_fwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* x, void* y, int64_t n) {
+    const int grid = grid_for(n, 256, sm_count * 4);
+    if (dt == HX_BF16)
+        gelu_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, (__nv_bfloat16*)y, n);
+    else
+        gelu_fwd_kernel<float><<<grid, 256, 0, st>>>((const float*)x, (float*)y, n);
+    note_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t gelu_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* g, const void* x, void* dx, int64_t n) {
+    const int grid = grid_for(n, 256, sm_count * 4);
+    if (dt == HX_BF16)
+        gelu_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)g, (const __nv_bfloat16*)x,
+                                                            (__nv_bfloat16*)dx, n);
+    else
+        gelu_bwd_kernel<float><<<grid, 256, 0, st>>>((const float*)g, (const float*)x, (float*)dx, n);
     note_launch();
     return cudaGetLastError();
 }

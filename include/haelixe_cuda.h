@@ -31,6 +31,16 @@
  *                                        and the matmul/add backward it records
  *   hx_rmsnorm_fwd / hx_rmsnorm_bwd   <- rms_norm_forward / rms_norm_backward
  *                                        (src/kernels/rms_norm.rs:20-132)
+ *   hx_gelu_fwd / hx_gelu_bwd         <- gelu / gelu_backward
+ *                                        (src/kernels/activations.rs:192-237)
+ *   hx_linear_residual_fwd            <- Linear::forward followed by the residual
+ *                                        add of TransformerBlock::forward
+ *                                        (src/nn/transformer.rs:26-40)
+ *   hx_cross_entropy                  <- Tensor::cross_entropy (src/tensor.rs:754-801)
+ *                                        with cross_entropy_forward/_backward
+ *                                        (src/kernels/loss.rs:46-117)
+ *   hx_adamw_step                     <- AdamW::step (src/optim.rs:128-199)
+ *   hx_embedding_fwd / _bwd              a token embedding (the reference has none)
  *   hx_attn_bwd_rope_strided          <- FlashAttentionOp::backward followed by
  *                                        rope_backward of dq and dk (the rope ->
  *                                        attention order of src/nn/attention.rs:76-78)
@@ -222,6 +232,62 @@ int hx_rmsnorm_fwd(hx_ctx* ctx, hx_dtype dtype, const void* x, const void* w, vo
  * over the rows. hidden <= 16384. */
 int hx_rmsnorm_bwd(hx_ctx* ctx, hx_dtype dtype, const void* dy, const void* x, const void* w, void* dx,
                    float* dw, int rows, int hidden, float eps);
+
+/* GELU, tanh form, element-wise over n elements (src/kernels/activations.rs:192-209),
+ * used by FeedForward (src/nn/mlp.rs); x and y may alias. */
+int hx_gelu_fwd(hx_ctx* ctx, hx_dtype dtype, const void* x, void* y, uint64_t n);
+/* Its exact derivative times dy (activations.rs:211-237). */
+int hx_gelu_bwd(hx_ctx* ctx, hx_dtype dtype, const void* dy, const void* x, void* dx, uint64_t n);
+
+/* ---- the training step around the block stack (src/nn/transformer.rs, src/optim.rs) --- */
+/* y = residual + x w + b: Linear::forward followed by TransformerBlock's
+ * residual add (src/nn/transformer.rs:32, 37); b and residual may be NULL,
+ * residual may alias y. Same layout and arithmetic as hx_linear_fwd. Its
+ * backward is hx_linear_bwd plus d(residual) = dy. */
+int hx_linear_residual_fwd(hx_ctx* ctx, hx_dtype dtype, const void* x, const void* w, const void* b,
+                           const void* residual, void* y, int rows, int in_features, int out_features);
+
+/* Mean cross-entropy of logits[rows, classes] (row-major) against targets[rows]
+ * (src/kernels/loss.rs:46-82): loss[0] = mean over rows of logsumexp(row) -
+ * row[target], written to device memory. When dlogits is not NULL it also
+ * writes the gradient of that mean, (softmax(row) - onehot(target)) / rows
+ * (loss.rs:86-117; like ops/cross_entropy.rs the upstream gradient is taken
+ * as 1), in `dtype`. A target >= classes makes the loss NaN (the reference
+ * panics on the out-of-range index). */
+int hx_cross_entropy(hx_ctx* ctx, hx_dtype dtype, const void* logits, const uint32_t* targets, float* loss,
+                     void* dlogits, int rows, int classes);
+
+/* One tensor of an AdamW step: f32 master weights and moments, the gradient in
+ * grad_dtype, and an optional bf16 copy of the updated weights (NULL for none)
+ * for bf16 storage with f32 master weights. */
+typedef struct hx_adamw_tensor {
+    float* param;
+    const void* grad;
+    float* m;
+    float* v;
+    void* param_lowp;
+    uint64_t n;
+    int32_t grad_dtype; /* hx_dtype */
+    int32_t reserved;   /* 0 */
+} hx_adamw_tensor;
+
+/* AdamW::step (src/optim.rs:128-199) over `count` tensors with step number
+ * `step` >= 1 (the reference's step_count after its increment): decoupled
+ * weight decay, then the moment updates and the bias-corrected step, each
+ * element in the reference's order and rounding. m and v start as zeros (the
+ * caller allocates them). bc1 = 1 - beta1^step and bc2 = 1 - beta2^step are
+ * formed on the host by f32 binary exponentiation, as Rust's f32::powi. */
+int hx_adamw_step(hx_ctx* ctx, const hx_adamw_tensor* tensors, int count, float lr, float beta1, float beta2,
+                  float eps, float weight_decay, int step);
+
+/* out[t, :] = table[ids[t], :] for t < tokens; table [vocab, dim] row-major.
+ * An id >= vocab writes a NaN row. */
+int hx_embedding_fwd(hx_ctx* ctx, hx_dtype dtype, const void* table, const uint32_t* ids, void* out,
+                     uint64_t tokens, int vocab, int dim);
+/* dtable[ids[t], :] += dout[t, :] in f32 (dtable is accumulated into, not
+ * cleared); ids >= vocab are skipped. */
+int hx_embedding_bwd(hx_ctx* ctx, hx_dtype dtype, const void* dout, const uint32_t* ids, float* dtable,
+                     uint64_t tokens, int vocab, int dim);
 
 /* ---- multi-GPU head sharding ------------------------------------------------------ */
 /* After an all-gather of per-rank head shards, shards holds n_shards

@@ -218,3 +218,88 @@ void ora_rms_norm_bwd(const float* g, const float* x, const float* w, float* dx,
         }
     }
 }
+
+/* GELU, tanh form, src/kernels/activations.rs:192-209:
+ * c = sqrt(2/pi), inner = c (x + 0.044715 x^3), y = 0.5 x (1 + tanh(inner)). */
+void ora_gelu_fwd(const float* x, float* y, long n) {
+    const float c = sqrtf(2.0f / 3.14159265358979323846f) /* std::f32::consts::PI */;
+    for (long i = 0; i < n; ++i) {
+        const float v = x[i];
+        const float inner = c * (v + 0.044715f * (v * v * v));
+        y[i] = 0.5f * v * (1.0f + tanhf(inner));
+    }
+}
+
+/* Its derivative times g, activations.rs:211-237:
+ * sech2 = 1 - tanh^2, d_inner = c (1 + 3 * 0.044715 x^2),
+ * dx = g (0.5 (1 + tanh) + 0.5 x sech2 d_inner). */
+void ora_gelu_bwd(const float* g, const float* x, float* dx, long n) {
+    const float c = sqrtf(2.0f / 3.14159265358979323846f) /* std::f32::consts::PI */;
+    for (long i = 0; i < n; ++i) {
+        const float v = x[i];
+        const float inner = c * (v + 0.044715f * (v * v * v));
+        const float t = tanhf(inner);
+        const float sech2 = 1.0f - t * t;
+        const float d_inner = c * (1.0f + 3.0f * 0.044715f * (v * v));
+        dx[i] = g[i] * (0.5f * (1.0f + t) + 0.5f * v * sech2 * d_inner);
+    }
+}
+
+/* Cross-entropy forward, src/kernels/loss.rs:46-82: per row the max, the sum
+ * of exp(x - max), lse = ln(sum) + max, loss = lse - x[target]; probs =
+ * exp(x - max) / sum; returns the mean of the row losses. Targets must be
+ * < classes (the reference panics otherwise). */
+float ora_cross_entropy_fwd(const float* logits, const uint32_t* targets, float* probs, long rows, long classes) {
+    float total = 0.0f;
+    for (long r = 0; r < rows; ++r) {
+        const float* row = logits + r * classes;
+        float mx = -INFINITY;
+        for (long j = 0; j < classes; ++j) mx = fmaxf(mx, row[j]);
+        float sum = 0.0f;
+        for (long j = 0; j < classes; ++j) sum += expf(row[j] - mx);
+        const float lse = logf(sum) + mx;
+        total += -row[targets[r]] + lse;
+        for (long j = 0; j < classes; ++j) probs[r * classes + j] = expf(row[j] - mx) / sum;
+    }
+    return total / (float)rows;
+}
+
+/* Cross-entropy backward, loss.rs:86-117: (probs - onehot) * (1 / rows). */
+void ora_cross_entropy_bwd(const float* probs, const uint32_t* targets, float* grads, long rows, long classes) {
+    const float scale = 1.0f / (float)rows;
+    for (long r = 0; r < rows; ++r)
+        for (long j = 0; j < classes; ++j) {
+            float g = probs[r * classes + j];
+            if ((uint32_t)j == targets[r]) g -= 1.0f;
+            grads[r * classes + j] = g * scale;
+        }
+}
+
+/* f32 a^n, n >= 0, by square-and-multiply: how Rust's f32::powi with a
+ * run-time exponent evaluates (llvm.powi). */
+static float powi_f32(float a, int n) {
+    float r = 1.0f;
+    for (;;) {
+        if (n & 1) r *= a;
+        n /= 2;
+        if (n == 0) break;
+        a *= a;
+    }
+    return r;
+}
+
+/* AdamW::step for one tensor, src/optim.rs:128-191, with `step` the
+ * step_count after the increment at optim.rs:130. */
+void ora_adamw_step(float* p, const float* g, float* m, float* v, long n, float lr, float beta1, float beta2,
+                    float eps, float weight_decay, int step) {
+    const float bc1 = 1.0f - powi_f32(beta1, step);
+    const float bc2 = 1.0f - powi_f32(beta2, step);
+    for (long i = 0; i < n; ++i) {
+        p[i] -= lr * weight_decay * p[i];
+        m[i] = beta1 * m[i] + (1.0f - beta1) * g[i];
+        v[i] = beta2 * v[i] + (1.0f - beta2) * g[i] * g[i];
+        const float m_hat = m[i] / bc1;
+        const float v_hat = v[i] / bc2;
+        p[i] -= lr * m_hat / (sqrtf(v_hat) + eps);
+    }
+}
