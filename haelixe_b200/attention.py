@@ -57,6 +57,7 @@ class CudaContext:
         st = N.lib().hx_ctx_create(self.device, ctypes.byref(h))
         N.check(st)
         self.handle = h.value
+        self._stream = None  # raw stream last handed to hx_ctx_set_stream
 
     def close(self) -> None:
         if self.handle:
@@ -70,8 +71,13 @@ class CudaContext:
             pass
 
     def use_stream(self, stream: Optional[torch.cuda.Stream] = None) -> None:
-        s = stream if stream is not None else torch.cuda.current_stream(self.device)
-        N.check(N.lib().hx_ctx_set_stream(self.handle, ctypes.c_void_p(s.cuda_stream)), self.handle)
+        """Enqueue the context's work on `stream` (default: torch's current
+        stream on this device). The library call is made only when the stream
+        changes."""
+        raw = stream.cuda_stream if stream is not None else torch._C._cuda_getCurrentRawStream(self.device)
+        if raw != self._stream:
+            N.check(N.lib().hx_ctx_set_stream(self.handle, ctypes.c_void_p(raw)), self.handle)
+            self._stream = raw
 
     def sync(self) -> None:
         N.check(N.lib().hx_sync(self.handle), self.handle)

@@ -686,7 +686,8 @@ int hx_linear_fwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w, const vo
     if ((st = blas_for(c, &h))) return st;
     float beta = 0.f;
     if (b != nullptr) {
-        if ((st = check_cuda(c, hx::bias_rows(c->stream, c->sm_count, dt, y, b, rows, out_features), "bias")))
+        if ((st = check_cuda(c, hx::rows_init(c->stream, c->sm_count, dt, y, nullptr, b, rows, out_features),
+                             "bias")))
             return st;
         beta = 1.f;
     }
@@ -715,7 +716,8 @@ int hx_linear_bwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w, const vo
         return st;
     if (db != nullptr) {  // db[out] = sum over rows of dy
         void* scratch = nullptr;
-        if ((st = hx_alloc(c, sizeof(float) * (uint64_t)out_features, &scratch))) return st;
+        if ((st = hx_alloc(c, sizeof(float) * (uint64_t)hx::col_scratch_floats(rows, out_features), &scratch)))
+            return st;
         st = check_cuda(c, hx::col_sum(c->stream, dt, dy, db, (float*)scratch, rows, out_features), "bias grad");
         hx_free(c, scratch);
     }
@@ -744,13 +746,17 @@ int hx_rmsnorm_bwd(hx_ctx* c, hx_dtype dt, const void* dy, const void* x, const 
     if (!dy || !x || !w || !dx || !dw) return set_error(c, HX_ERR_INVALID, "hx_rmsnorm_bwd: NULL operand");
     if (rows <= 0 || hidden <= 0 || !(eps >= 0.f))
         return set_error(c, HX_ERR_INVALID, "hx_rmsnorm_bwd: rows, hidden must be positive, eps >= 0");
-    if (hidden > 16384)
-        return set_error(c, HX_ERR_UNSUPPORTED, "hx_rmsnorm_bwd: hidden %d > 16384 is not supported", hidden);
     DeviceGuard g(c->device);
     NvtxRange nv("hx_rmsnorm_bwd");
     LaunchCount lc(c);
-    return check_cuda(c, hx::rmsnorm_bwd(c->stream, c->sm_count, dt, dy, x, w, dx, dw, rows, hidden, eps),
-                      "hx_rmsnorm_bwd");
+    void* scratch = nullptr;
+    if ((st = hx_alloc(c, sizeof(float) * (uint64_t)hx::rmsnorm_bwd_scratch_floats(rows, hidden), &scratch)))
+        return st;
+    st = check_cuda(c, hx::rmsnorm_bwd(c->stream, c->sm_count, dt, dy, x, w, dx, dw, (float*)scratch, rows, hidden,
+                                       eps),
+                    "hx_rmsnorm_bwd");
+    hx_free(c, scratch);
+    return st;
 }
 
 int hx_gelu_fwd(hx_ctx* c, hx_dtype dt, const void* x, void* y, uint64_t n) {
@@ -791,7 +797,7 @@ int hx_linear_residual_fwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w,
     if ((st = blas_for(c, &h))) return st;
     float beta = 0.f;
     if (b != nullptr || residual != nullptr) {
-        if ((st = check_cuda(c, hx::residual_bias(c->stream, c->sm_count, dt, y, residual, b, rows, out_features),
+        if ((st = check_cuda(c, hx::rows_init(c->stream, c->sm_count, dt, y, residual, b, rows, out_features),
                              "residual rows")))
             return st;
         beta = 1.f;

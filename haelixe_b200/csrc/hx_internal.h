@@ -99,8 +99,9 @@ cudaError_t sm100_attn_bwd(cudaStream_t st, int sm_count, DeviceStatus* status,
 cudaError_t rmsnorm_fwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* x, const void* w, void* y,
                         int rows, int hidden, float eps);
 cudaError_t rmsnorm_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* g, const void* x, const void* w,
-                        void* dx, float* dw, int rows, int hidden, float eps);
-cudaError_t bias_rows(cudaStream_t st, int sm_count, hx_dtype dt, void* y, const void* b, int64_t rows, int cols);
+                        void* dx, float* dw, float* scratch, int rows, int hidden, float eps);
+cudaError_t rows_init(cudaStream_t st, int sm_count, hx_dtype dt, void* y, const void* res, const void* b,
+                      int64_t rows, int cols);
 cudaError_t cross_entropy(cudaStream_t st, hx_dtype dt, const void* logits, const uint32_t* targets,
                           float* row_loss, float* loss, void* dlogits, int rows, int classes);
 cudaError_t adamw_step(cudaStream_t st, int sm_count, const hx_adamw_tensor* tensors, int count, float lr,
@@ -109,11 +110,12 @@ cudaError_t embedding_fwd(cudaStream_t st, int sm_count, hx_dtype dt, const void
                           void* out, int64_t tokens, int vocab, int dim);
 cudaError_t embedding_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* dout, const uint32_t* ids,
                           float* dtable, int64_t tokens, int vocab, int dim);
-cudaError_t residual_bias(cudaStream_t st, int sm_count, hx_dtype dt, void* y, const void* res, const void* b,
-                          int64_t rows, int cols);
 cudaError_t gelu_fwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* x, void* y, int64_t n);
 cudaError_t gelu_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* g, const void* x, void* dx, int64_t n);
+// db[c] = sum over rows of dy[r, c]; scratch holds col_scratch_floats(rows, cols) floats.
 cudaError_t col_sum(cudaStream_t st, hx_dtype dt, const void* dy, void* db, float* scratch, int64_t rows, int cols);
+int64_t col_scratch_floats(int64_t rows, int cols);
+int64_t rmsnorm_bwd_scratch_floats(int64_t rows, int hidden);
 
 // ---- failure-path self-test (selftest.cu) ----
 cudaError_t selftest_wait_timeout(cudaStream_t st, DeviceStatus* status);

@@ -1,9 +1,8 @@
 // Device kernels of the training step around the attention stack: the
 // cross-entropy loss (Tensor::cross_entropy, src/tensor.rs:754-801, with
-// src/kernels/loss.rs:46-117), the AdamW update (src/optim.rs:128-199), the
-// residual + bias rows of Linear (src/nn/linear.rs:54-56 followed by the
-// residual add of src/nn/transformer.rs:32-37) and a token embedding (the
-// reference has none; it gathers rows of a [vocab, hidden] table).
+// src/kernels/loss.rs:46-117), the AdamW update (src/optim.rs:128-199) and a
+// token embedding (the reference has none; it gathers rows of a
+// [vocab, hidden] table).
 //
 // All of them are HBM-bound integer/element work: coalesced 4- and 16-byte
 // accesses, grids sized to the SM count, no tensor cores.
@@ -49,22 +48,71 @@ __device__ __forceinline__ void ms_merge(float& m, float& s, float m2, float s2)
     }
 }
 
+// 16-byte loads of 8 bf16 / 4 f32 logits as f32.
 template <typename T>
+__device__ __forceinline__ void vld16(const T* p, float (&f)[16 / sizeof(T)]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    if constexpr (sizeof(T) == 4) {
+        f[0] = __uint_as_float(u.x), f[1] = __uint_as_float(u.y);
+        f[2] = __uint_as_float(u.z), f[3] = __uint_as_float(u.w);
+    } else {
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+            f[2 * i] = t.x, f[2 * i + 1] = t.y;
+        }
+    }
+}
+template <typename T>
+__device__ __forceinline__ void vst16(T* p, const float (&f)[16 / sizeof(T)]) {
+    uint4 u;
+    if constexpr (sizeof(T) == 4) {
+        u.x = __float_as_uint(f[0]), u.y = __float_as_uint(f[1]);
+        u.z = __float_as_uint(f[2]), u.w = __float_as_uint(f[3]);
+    } else {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        u.x = w[0], u.y = w[1], u.z = w[2], u.w = w[3];
+    }
+    *reinterpret_cast<uint4*>(p) = u;
+}
+
+// exp of arguments <= 0 (logit - running max) with the hardware exp2
+// (__expf): a few 1e-7 relative, far inside the loss's tolerance.
+__device__ __forceinline__ void ms_add(float& m, float& s, float v) {
+    if (v > m) {
+        s = s * __expf(m - v) + 1.f;
+        m = v;
+    } else if (m != -INFINITY) {  // -inf logits add exp(-inf) = 0
+        s += __expf(v - m);
+    }
+}
+
+// VEC: 16-byte accesses (classes a multiple of 16 / sizeof(T), rows 16-byte aligned).
+template <typename T, bool VEC>
 __global__ void __launch_bounds__(CE_THREADS) cross_entropy_kernel(const T* __restrict__ logits,
                                                                    const uint32_t* __restrict__ targets,
                                                                    float* __restrict__ row_loss,
                                                                    T* __restrict__ dlogits, int rows, int classes) {
+    constexpr int N = VEC ? 16 / sizeof(T) : 1;
     __shared__ float sm[CE_THREADS / 32], ss[CE_THREADS / 32];
     const int r = blockIdx.x;
     const T* x = logits + (int64_t)r * classes;
+    const int nv = classes / N;
     float m = -INFINITY, s = 0.f;
-    for (int j = threadIdx.x; j < classes; j += CE_THREADS) {
-        const float v = ldf(x, j);
-        if (v > m) {
-            s = s * expf(m - v) + 1.f;
-            m = v;
-        } else if (m != -INFINITY) {  // -inf logits add exp(-inf) = 0
-            s += expf(v - m);
+    for (int j = threadIdx.x; j < nv; j += CE_THREADS) {
+        if constexpr (VEC) {
+            float v[N];
+            vld16(x + (int64_t)j * N, v);
+#pragma unroll
+            for (int k = 0; k < N; ++k) ms_add(m, s, v[k]);
+        } else {
+            ms_add(m, s, ldf(x, j));
         }
     }
 #pragma unroll
@@ -88,10 +136,22 @@ __global__ void __launch_bounds__(CE_THREADS) cross_entropy_kernel(const T* __re
     if (dlogits == nullptr) return;
     T* dx = dlogits + (int64_t)r * classes;
     const float inv_s = 1.f / s, inv_rows = 1.f / (float)rows;
-    for (int j = threadIdx.x; j < classes; j += CE_THREADS) {
-        float p = expf(ldf(x, j) - m) * inv_s;
-        if ((uint32_t)j == t) p -= 1.f;
-        stf(dx, j, p * inv_rows);
+    for (int j = threadIdx.x; j < nv; j += CE_THREADS) {
+        if constexpr (VEC) {
+            float v[N];
+            vld16(x + (int64_t)j * N, v);
+#pragma unroll
+            for (int k = 0; k < N; ++k) {
+                float p = __expf(v[k] - m) * inv_s;
+                if ((uint32_t)(j * N + k) == t) p -= 1.f;
+                v[k] = p * inv_rows;
+            }
+            vst16(dx + (int64_t)j * N, v);
+        } else {
+            float p = __expf(ldf(x, j) - m) * inv_s;
+            if ((uint32_t)j == t) p -= 1.f;
+            stf(dx, j, p * inv_rows);
+        }
     }
 }
 
@@ -249,27 +309,6 @@ __global__ void __launch_bounds__(256) embedding_bwd_kernel(const T* __restrict_
     }
 }
 
-// ---- residual + bias rows ----------------------------------------------------------
-// y[r, c] = res[r, c] + b[c] (either may be absent): the rows a GEMM with
-// beta = 1 then adds x w onto, which fuses Linear's bias add and the block's
-// residual add into the GEMM's epilogue.
-template <typename T>
-__global__ void __launch_bounds__(256) residual_bias_kernel(T* __restrict__ y, const T* __restrict__ res,
-                                                            const T* __restrict__ b, int64_t rows, int cols) {
-    const int64_t n = rows * cols;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        float v = res ? ldf(res, i) : 0.f;
-        if (b) v += ldf(b, i % cols);
-        stf(y, i, v);
-    }
-}
-
-__global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restrict__ a, __nv_bfloat16* __restrict__ o,
-                                                         int64_t n) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        o[i] = __float2bfloat16_rn(a[i]);
-}
-
 int grid_cap(int64_t work, int per_block, int cap) {
     int64_t b = (work + per_block - 1) / per_block;
     if (b > cap) b = cap;
@@ -280,12 +319,26 @@ int grid_cap(int64_t work, int per_block, int cap) {
 
 cudaError_t cross_entropy(cudaStream_t st, hx_dtype dt, const void* logits, const uint32_t* targets,
                           float* row_loss, float* loss, void* dlogits, int rows, int classes) {
-    if (dt == HX_BF16)
-        cross_entropy_kernel<__nv_bfloat16><<<rows, CE_THREADS, 0, st>>>(
-            (const __nv_bfloat16*)logits, targets, row_loss, (__nv_bfloat16*)dlogits, rows, classes);
-    else
-        cross_entropy_kernel<float><<<rows, CE_THREADS, 0, st>>>((const float*)logits, targets, row_loss,
-                                                                 (float*)dlogits, rows, classes);
+    const int n16 = dt == HX_BF16 ? 8 : 4;
+    const bool vec = classes % n16 == 0 && ((reinterpret_cast<uintptr_t>(logits) |
+                                              reinterpret_cast<uintptr_t>(dlogits)) & 15) == 0;
+    if (dt == HX_BF16) {
+        auto* lg = (const __nv_bfloat16*)logits;
+        auto* dl = (__nv_bfloat16*)dlogits;
+        if (vec)
+            cross_entropy_kernel<__nv_bfloat16, true><<<rows, CE_THREADS, 0, st>>>(lg, targets, row_loss, dl, rows,
+                                                                                  classes);
+        else
+            cross_entropy_kernel<__nv_bfloat16, false><<<rows, CE_THREADS, 0, st>>>(lg, targets, row_loss, dl, rows,
+                                                                                   classes);
+    } else {
+        if (vec)
+            cross_entropy_kernel<float, true><<<rows, CE_THREADS, 0, st>>>((const float*)logits, targets, row_loss,
+                                                                          (float*)dlogits, rows, classes);
+        else
+            cross_entropy_kernel<float, false><<<rows, CE_THREADS, 0, st>>>((const float*)logits, targets, row_loss,
+                                                                           (float*)dlogits, rows, classes);
+    }
     note_launch();
     mean_kernel<<<1, 1024, 0, st>>>(row_loss, loss, rows);
     note_launch();
@@ -345,26 +398,6 @@ cudaError_t embedding_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void
                                                                  vocab, dim);
     else
         embedding_bwd_kernel<float><<<grid, 256, 0, st>>>((const float*)dout, ids, dtable, tokens, vocab, dim);
-    note_launch();
-    return cudaGetLastError();
-}
-
-cudaError_t residual_bias(cudaStream_t st, int sm_count, hx_dtype dt, void* y, const void* res, const void* b,
-                          int64_t rows, int cols) {
-    const int grid = grid_cap(rows * cols, 256, sm_count * 8);
-    if (dt == HX_BF16)
-        residual_bias_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((__nv_bfloat16*)y, (const __nv_bfloat16*)res,
-                                                                 (const __nv_bfloat16*)b, rows, cols);
-    else
-        residual_bias_kernel<float><<<grid, 256, 0, st>>>((float*)y, (const float*)res, (const float*)b, rows,
-                                                         cols);
-    note_launch();
-    return cudaGetLastError();
-}
-
-cudaError_t f32_to_bf16(cudaStream_t st, int sm_count, const float* a, void* out, int64_t n) {
-    const int grid = grid_cap(n, 256, sm_count * 8);
-    f32_to_bf16_kernel<<<grid, 256, 0, st>>>(a, (__nv_bfloat16*)out, n);
     note_launch();
     return cudaGetLastError();
 }

@@ -229,7 +229,7 @@ int hx_linear_bwd(hx_ctx* ctx, hx_dtype dtype, const void* x, const void* w, con
 int hx_rmsnorm_fwd(hx_ctx* ctx, hx_dtype dtype, const void* x, const void* w, void* y, int rows,
                    int hidden, float eps);
 /* Its backward (src/kernels/rms_norm.rs:57-132): dx, and dw in f32 summed
- * over the rows. hidden <= 16384. */
+ * over the rows. */
 int hx_rmsnorm_bwd(hx_ctx* ctx, hx_dtype dtype, const void* dy, const void* x, const void* w, void* dx,
                    float* dw, int rows, int hidden, float eps);
 

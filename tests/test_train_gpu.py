@@ -305,3 +305,46 @@ def test_block_stack_step_matches_oracle(dtype):
             assert np.array_equal(_np(q), rp)
         else:
             assert np.array_equal(_np(q), ora.round_bf16(rp))
+
+
+@pytest.mark.parametrize("dtype", DT)
+@pytest.mark.parametrize("rows,fin,fout", [(70, 100, 75), (33, 64, 8), (1, 9, 3)])
+def test_row_kernels_vector_and_scalar_forms(dtype, rows, fin, fout):
+    """RMSNorm, Linear (+ residual, bias gradient) and GELU on widths that are
+    and are not multiples of the 16-byte vector, with tiles of rows that do
+    not fill a block, against the oracle."""
+    rng = np.random.default_rng(rows * 1000 + fin)
+    x = _rnd(rng.standard_normal((rows, fin)).astype(np.float32), dtype)
+    nw = _rnd(rng.uniform(0.5, 1.5, fin).astype(np.float32), dtype)
+    gn = _rnd(rng.standard_normal((rows, fin)).astype(np.float32), dtype)
+    w = _rnd(rng.standard_normal((fin, fout)).astype(np.float32) * 0.1, dtype)
+    b = _rnd(rng.standard_normal(fout).astype(np.float32), dtype)
+    r = _rnd(rng.standard_normal((rows, fout)).astype(np.float32), dtype)
+    g = _rnd(rng.standard_normal((rows, fout)).astype(np.float32), dtype)
+    tol = 1e-3 if dtype == F32 else 3e-2
+
+    def close(name, got, ref):
+        err = np.abs(_np(got) - ref).max() / max(1.0, np.abs(ref).max())
+        assert err < tol, (name, err)
+
+    xt, nwt = _dev(x, dtype, grad=True), _dev(nw, dtype, grad=True)
+    n = hx.nn.rms_norm(xt, nwt)
+    n.backward(_dev(gn, dtype))
+    rdx, rdw = ora.rms_norm_bwd(gn, x, nw)
+    close("norm", n, ora.rms_norm_fwd(x, nw))
+    close("norm dx", xt.grad, rdx)
+    close("norm dw", nwt.grad, rdw)
+
+    xt2, wt, bt, rt = (_dev(a, dtype, grad=True) for a in (x, w, b, r))
+    y = hx.nn.linear(xt2, wt, bt, residual=rt)
+    y.backward(_dev(g, dtype))
+    close("y", y, r + (ora.matmul(x, w) + b))
+    close("db", bt.grad, g.sum(0))
+    close("dw", wt.grad, ora.matmul(np.ascontiguousarray(x.T), g))
+
+    # GELU on an unaligned view (one element in): the scalar form
+    buf = _dev(np.concatenate([[0.0], x.reshape(-1)]).astype(np.float32), dtype)
+    xv = buf[1:].detach().requires_grad_()
+    gy = hx.nn.gelu(xv)
+    gy.backward(_dev(gn.reshape(-1)[: x.size] if gn.size >= x.size else np.ones(x.size, np.float32), dtype))
+    close("gelu", gy, ora.gelu_fwd(x.reshape(-1)))
