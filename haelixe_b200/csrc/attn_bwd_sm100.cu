@@ -116,6 +116,11 @@ struct BBars {
 
 static_assert(sizeof(BBars) <= 256, "barrier block");
 
+// (batch, head) slices per dispatch group of the backward grid.
+#ifndef HX_BWD_HGROUP
+#define HX_BWD_HGROUP 2
+#endif
+
 struct BwdParams {
     const float* lse2;   // [B*H][S_pad]: lse * log2(e), 0 past S
     const float* delta;  // [B*H][S_pad]: rowsum(dO * O), 0 past S
@@ -130,6 +135,7 @@ struct BwdParams {
     // the kernel rotated back by -theta of its key row: the gradient with
     // respect to K before the rotary embedding (src/kernels/rope.rs:44-82).
     const float2* rope_tab;
+    int hgroup;  // (batch, head) slices per dispatch group (see the block mapping)
     DeviceStatus* status;
 };
 
@@ -164,8 +170,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* s_lse = (float*)(sm + C::LSE_OFF);
     float* s_del = (float*)(sm + C::DEL_OFF);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int k0 = blockIdx.x * BK;
-    const int h = blockIdx.y, b = blockIdx.z;
+    // 1D grid in groups of hgroup (batch, head) slices; inside a group the
+    // key block varies slowest. Blocks are dispatched in index order, so with
+    // causal masking the group's heaviest (first) key blocks go first and the
+    // light ones fill the tail (longest first within a group), while the
+    // blocks in flight stream only a group's worth of Q, dO and dQ (L2).
+    const int nblk = (p.S + BK - 1) / BK;
+    const int nbh = (int)(gridDim.x / nblk);
+    const int grp = (int)(blockIdx.x / ((unsigned)p.hgroup * nblk));
+    const int gs = min(p.hgroup, nbh - grp * p.hgroup);
+    const int loc = (int)(blockIdx.x - (unsigned)grp * p.hgroup * nblk);
+    const int kb = loc / gs, bhi = grp * p.hgroup + loc % gs;
+    const int k0 = kb * BK;
+    const int h = bhi % p.H, b = bhi / p.H;
     const int64_t bh = (int64_t)b * p.H + h;
     const int i_start = p.causal ? k0 / BQ : 0;
     const int n_it = (p.S + BQ - 1) / BQ - i_start;
@@ -792,8 +809,9 @@ cudaError_t launch(cudaStream_t st, int sm_count, DeviceStatus* status, const At
     prm.scale = scale;
     prm.causal = causal;
     prm.rope_tab = rope_tab;
+    prm.hgroup = HX_BWD_HGROUP;
     prm.status = status;
-    dim3 grid((d.S + BK - 1) / BK, d.H, d.B);
+    dim3 grid((unsigned)((d.S + BK - 1) / BK * d.H * d.B));
     attn_bwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, tdo, tdq, prm);
     note_launch();
     e = cudaGetLastError();

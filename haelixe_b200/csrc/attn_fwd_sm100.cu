@@ -84,6 +84,11 @@ struct Bars {
     int abort_flag;
 };
 
+// (batch, head) slices per dispatch group of the forward grid.
+#ifndef HX_FWD_HGROUP
+#define HX_FWD_HGROUP 8
+#endif
+
 struct FwdParams {
     __nv_bfloat16* o;
     float* lse;
@@ -91,6 +96,7 @@ struct FwdParams {
     int S, H;
     float sl2;  // scale * log2(e)
     int causal;
+    int hgroup;  // (batch, head) slices per dispatch group (see the block mapping)
     DeviceStatus* status;
 };
 
@@ -111,9 +117,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     B* bars = (B*)(sm + C::BAR_OFF);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
-    const int mblk = p.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    // 1D grid in groups of hgroup (batch, head) slices; inside a group the
+    // query block varies slowest. The hardware dispatches blocks in index
+    // order, so with causal masking the group's heaviest (last) query blocks
+    // of all its slices go first and the light ones fill the tail: longest
+    // first within a group (even load at the end of the grid), while the
+    // blocks in flight touch only a group's worth of K/V (L2 locality).
+    const int nblk = (p.S + NWG * BM - 1) / (NWG * BM);
+    const int nbh = (int)(gridDim.x / nblk);
+    const int grp = (int)(blockIdx.x / ((unsigned)p.hgroup * nblk));
+    const int gs = min(p.hgroup, nbh - grp * p.hgroup);
+    const int loc = (int)(blockIdx.x - (unsigned)grp * p.hgroup * nblk);
+    const int qi = loc / gs, bhi = grp * p.hgroup + loc % gs;
+    const int mblk = p.causal ? nblk - 1 - qi : qi;
     const int m0 = mblk * (NWG * BM);
-    const int h = blockIdx.y, b = blockIdx.z;
+    const int h = bhi % p.H, b = bhi / p.H;
     const int n_all = (p.S + BN - 1) / BN;
     int n_w[NWG];
 #pragma unroll
@@ -485,8 +503,9 @@ cudaError_t launch(cudaStream_t st, DeviceStatus* status, const AttnDims& d, con
     prm.H = d.H;
     prm.sl2 = scale * kLog2e;
     prm.causal = causal;
+    prm.hgroup = HX_FWD_HGROUP;
     prm.status = status;
-    dim3 grid((d.S + NWG * BM - 1) / (NWG * BM), d.H, d.B);
+    dim3 grid((unsigned)((d.S + NWG * BM - 1) / (NWG * BM) * d.H * d.B));
     attn_fwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, prm);
     note_launch();
     return cudaGetLastError();
