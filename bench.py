@@ -40,10 +40,10 @@ UNIT = "TFLOP/s"
 FALLBACK_PEAK_TFLOPS = 1590.0
 # DRAM bytes (read + write) per launch of the dominant kernel (the tcgen05
 # backward) at B4 H32 S8192 D128: an ncu capture of the same kernel at B1
-# (profiles/attn_bwd_kernel_B1_H32_S8192_D128.md: 413.9 MB read + 226.0 MB
+# (profiles/attn_bwd_kernel_B1_H32_S8192_D128.md: 414.0 MB read + 225.6 MB
 # written) scaled by 4, since the heads are independent and the traffic grows
 # with B*H. Valid for the default workload only; other shapes report None.
-DOMINANT_KERNEL_TRAFFIC_BYTES = 4 * (413.910528e6 + 226.01728e6)
+DOMINANT_KERNEL_TRAFFIC_BYTES = 4 * (414.047232e6 + 225.557248e6)
 TRAFFIC_WORKLOAD = (4, 32, 8192, 128)
 
 
