@@ -69,7 +69,7 @@ def parse():
     p.add_argument("--no-causal", action="store_true")
     p.add_argument("--rope-theta", type=float, default=500000.0)
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--e2e-steps", type=int, default=6)
+    p.add_argument("--e2e-steps", type=int, default=20)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--workload", choices=["attention", "block_stack"], default="attention")
@@ -441,9 +441,12 @@ def e2e_measure(a, ctx, N, torch, dev, world, sets, step, total_flops):
     launch stream, copies out on a third, over two device buffer sets, so step
     i's results go out while step i+1's inputs come in (PCIe is full duplex)
     and the compute overlaps both. Every step moves all of its bytes inside the
-    timed region."""
+    timed region. The timed window runs from the first step's first upload to
+    the last step's last download, so it includes the pipeline's fill and
+    drain (one un-overlapped upload and download); 20 steps keep those to a
+    few percent of the window (about 0.5 s at the attention workload)."""
     import ctypes
-    steps = max(2, min(a.e2e_steps, a.steps))
+    steps = max(2, a.e2e_steps)
     ins, outs = ("q", "k", "v", "do"), ("o", "dq0", "dk0", "dv")
     h_in = [torch.empty(sets[0][n].shape, dtype=sets[0][n].dtype, pin_memory=True) for n in ins]
     for h, n in zip(h_in, ins):
