@@ -264,8 +264,11 @@ def test_autograd_node_with_rope():
     _check("dV", vd.grad, rdv, torch.bfloat16)
 
 
-def _sampled_full_size(B, H, S, D, causal, rope_base=None, samples=((0, 0),)):
-    """Full-size run on the GPU; oracle on sampled (b, h) slices; identities on all."""
+def _sampled_full_size(B, H, S, D, causal, rope_base=None, samples=((0, 0),), prefix=None):
+    """Full-size run on the GPU; oracle on sampled (b, h) slices; identities on all.
+    With `prefix` (causal only) the sampled slices are checked on their first
+    `prefix` rows instead: under the causal mask, O and dQ of query rows
+    < prefix depend only on keys < prefix, so the oracle runs on the prefix."""
     torch.manual_seed(0)
     g = torch.Generator(device="cuda").manual_seed(1234)
     q, k, v, do = (torch.randn(B, H, S, D, device="cuda", generator=g).to(torch.bfloat16)
@@ -284,6 +287,14 @@ def _sampled_full_size(B, H, S, D, causal, rope_base=None, samples=((0, 0),)):
     dv_l1 = dv.float().abs().sum(2)
     assert ((dvs - dos).abs() <= 0.02 * dv_l1 + 1e-2).all(), ((dvs - dos).abs() / dv_l1).max().item()
     for (b, h) in samples:
+        if prefix is not None:
+            assert causal
+            sl = [t[b, h, :prefix].float().cpu().numpy()[None] for t in (q, k, v, do)]
+            ro, _ = ora.attn_fwd(*sl[:3], scale, causal)
+            rdq = ora.attn_bwd(*sl, scale, causal)[0]
+            _check(f"O[{b},{h},:{prefix}]", o[b, h, :prefix], ro[0], torch.bfloat16)
+            _check(f"dQ[{b},{h},:{prefix}]", dq[b, h, :prefix], rdq[0], torch.bfloat16)
+            continue
         sl = [t[b, h].float().cpu().numpy()[None] for t in (q, k, v, do)]
         ro, _ = ora.attn_fwd(*sl[:3], scale, causal)
         rg = ora.attn_bwd(*sl, scale, causal)
@@ -298,6 +309,13 @@ def test_standalone_op_b8_h16_s2048_d64_causal():
 
 def test_llama_layer_b4_h32_s8192_d128_causal_rope():
     _sampled_full_size(4, 32, 8192, 128, True, rope_base=500000.0, samples=((3, 31),))
+
+
+def test_long_context_b1_h64_s32768_d128_causal():
+    """The long-context configuration at full size (64 heads x 32768): the
+    gradient identities on every head, and O and dQ of the first 2048 query
+    rows of two heads against the oracle (causal prefix consistency)."""
+    _sampled_full_size(1, 64, 32768, 128, True, samples=((0, 0), (0, 63)), prefix=2048)
 
 
 def test_full_mask_long_sequences():
