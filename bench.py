@@ -344,6 +344,13 @@ def run_haelixe(a):
             comm.wait_event(done)
             with torch.cuda.stream(comm):
                 dist.all_gather_into_tensor(gathered, o.reshape(-1))
+                # The reassembly needs only the gather: it runs on the same side
+                # stream, beside the backward, instead of after it.
+                ctx.use_stream()
+                N.check(N.lib().hx_reassemble_heads(ctx.handle, N.HX_BF16, gathered.data_ptr(),
+                                                    merged.data_ptr(), world, B, Hl, S, D, 1),
+                        ctx.handle)
+            ctx.use_stream()
         # Backward with the rotary embedding's backward fused into the last
         # writes of dQ and dK: dq0, dk0 are the gradients of q, k before RoPE.
         hx.attn_backward(qr, kr, v, o, lse, do, scale, causal, dq=dq0, dk=dk0, dv=dv,
@@ -351,15 +358,23 @@ def run_haelixe(a):
         if timed:
             ev["b1"][-1].record(stream)
         if world > 1:
-            stream.wait_stream(comm)
-            N.check(N.lib().hx_reassemble_heads(ctx.handle, N.HX_BF16, gathered.data_ptr(),
-                                                merged.data_ptr(), world, B, Hl, S, D, 1),
-                    ctx.handle)
+            stream.wait_stream(comm)  # the step ends with O gathered and merged on every rank
 
     for _ in range(a.warmup):
         step()
     torch.cuda.synchronize()
     if world > 1:
+        # Untimed check of the gathered output: this rank's heads of `merged`
+        # are its own O, and every rank holds the same merged tensor.
+        own = torch.equal(merged[:, :, rank * Hl:(rank + 1) * Hl], o.transpose(1, 2))
+        cs = merged.float().sum(dtype=torch.float64).reshape(1)
+        lo, hi = cs.clone(), cs.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        ok = torch.tensor([1 if (own and lo.item() == hi.item()) else 0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if ok.item() != 1:
+            raise SystemExit(f"rank {rank}: gathered heads do not match (own slice {own})")
         dist.barrier()
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
