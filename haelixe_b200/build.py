@@ -1,8 +1,10 @@
-"""Builds haelixe_b200/lib/libhaelixe_cuda.so from csrc/ with nvcc for sm_100a.
+"""Builds haelixe_b200/lib/libhaelixe_cuda.so from csrc/ with nvcc for sm_100a,
+and the C++ host layer over it (host/ -> lib/libhaelixe_host.so, with g++).
 
-The library is the product: the C ABI of include/haelixe_cuda.h over the
-hand-written CUDA kernels. Objects go to haelixe_b200/_build/ and are rebuilt
-when their source or any header is newer.
+The CUDA library is the product: the C ABI of include/haelixe_cuda.h over the
+hand-written CUDA kernels. The host layer mirrors the crate's Tensor / Device /
+FlashAttentionOp types above that ABI. Objects go to haelixe_b200/_build/ and
+are rebuilt when their source or any header is newer.
 """
 from __future__ import annotations
 
@@ -17,6 +19,8 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libhaelixe_cuda.so")
+HOST_DIR = os.path.join(HERE, "host")
+HOST_LIB = os.path.join(LIB_DIR, "libhaelixe_host.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -77,7 +81,22 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     if force or jobs or _stale(LIB, objs):
         cmd = [nvcc] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart", "-lcublas"]
         run(cmd)
+    build_host(force)
     return LIB
+
+
+def build_host(force: bool = False) -> str:
+    """The C++ host layer: plain C++17 over the C ABI, linked to the CUDA library."""
+    srcs = sorted(glob.glob(os.path.join(HOST_DIR, "*.cpp")))
+    deps = srcs + glob.glob(os.path.join(HOST_DIR, "*.hpp")) + glob.glob(os.path.join(INCLUDE, "*.h")) + [LIB]
+    if force or _stale(HOST_LIB, deps):
+        cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
+        cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-Wextra", "-I", INCLUDE, "-I", HOST_DIR,
+               *srcs, "-L", LIB_DIR, "-lhaelixe_cuda", "-Wl,-rpath,$ORIGIN", "-o", HOST_LIB]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"host build failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    return HOST_LIB
 
 
 if __name__ == "__main__":
