@@ -100,6 +100,7 @@ SIGNATURES = {
     "hx_adamw_step": (_I, [_P, _P, _I, _F, _F, _F, _F, _F, _I]),
     "hx_embedding_fwd": (_I, [_P, _I, _P, _P, _P, _U64, _I, _I]),
     "hx_embedding_bwd": (_I, [_P, _I, _P, _P, _P, _U64, _I, _I]),
+    "hx_add": (_I, [_P, _I, _P, _P, _P, _U64]),
     "hx_gelu_fwd": (_I, [_P, _I, _P, _P, _U64]),
     "hx_gelu_bwd": (_I, [_P, _I, _P, _P, _P, _U64]),
     "hx_rope_fwd": (_I, [_P, _I, _SHP, _P, _P, _F]),

@@ -771,6 +771,18 @@ int hx_gelu_fwd(hx_ctx* c, hx_dtype dt, const void* x, void* y, uint64_t n) {
     return check_cuda(c, hx::gelu_fwd(c->stream, c->sm_count, dt, x, y, (int64_t)n), "hx_gelu_fwd");
 }
 
+int hx_add(hx_ctx* c, hx_dtype dt, const void* a, const void* b, void* out, uint64_t n) {
+    if (c == nullptr) return HX_ERR_INVALID;
+    int st;
+    if ((st = validate_dtype(c, dt, "hx_add"))) return st;
+    if (!a || !b || !out) return set_error(c, HX_ERR_INVALID, "hx_add: NULL operand");
+    if (n == 0) return HX_OK;
+    DeviceGuard g(c->device);
+    NvtxRange nv("hx_add");
+    LaunchCount lc(c);
+    return check_cuda(c, hx::add(c->stream, c->sm_count, dt, a, b, out, (int64_t)n), "hx_add");
+}
+
 int hx_gelu_bwd(hx_ctx* c, hx_dtype dt, const void* dy, const void* x, void* dx, uint64_t n) {
     if (c == nullptr) return HX_ERR_INVALID;
     int st;

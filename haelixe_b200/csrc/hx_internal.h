@@ -111,6 +111,7 @@ cudaError_t embedding_fwd(cudaStream_t st, int sm_count, hx_dtype dt, const void
 cudaError_t embedding_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* dout, const uint32_t* ids,
                           float* dtable, int64_t tokens, int vocab, int dim);
 cudaError_t gelu_fwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* x, void* y, int64_t n);
+cudaError_t add(cudaStream_t st, int sm_count, hx_dtype dt, const void* a, const void* b, void* out, int64_t n);
 cudaError_t gelu_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* g, const void* x, void* dx, int64_t n);
 // db[c] = sum over rows of dy[r, c]; scratch holds col_scratch_floats(rows, cols) floats.
 cudaError_t col_sum(cudaStream_t st, hx_dtype dt, const void* dy, void* db, float* scratch, int64_t rows, int cols);

@@ -361,6 +361,30 @@ __global__ void __launch_bounds__(256) gelu_bwd_kernel(const T* __restrict__ g, 
     for (int64_t i = nv * N + t0; i < n; i += stride) st(dx, i, gelu_d<(sizeof(T) == 2)>(ld(g, i), ld(x, i)));
 }
 
+// out = a + b element-wise (kernels/binary.rs:40-60 for equal shapes: the
+// gradient accumulation of the autograd walk, tensor.rs:211-214); out may
+// alias a or b.
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) add_kernel(const T* a, const T* b, T* out, int64_t n) {
+    constexpr int N = VEC ? Vec<T>::N : 1;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t nv = n / N;
+    for (int64_t i = t0; i < nv; i += stride) {
+        if constexpr (VEC) {
+            float x[N], y[N];
+            vld(a + i * N, x);
+            vld(b + i * N, y);
+#pragma unroll
+            for (int k = 0; k < N; ++k) x[k] += y[k];
+            vst(out + i * N, x);
+        } else {
+            st(out, i, ld(a, i) + ld(b, i));
+        }
+    }
+    for (int64_t i = nv * N + t0; i < n; i += stride) st(out, i, ld(a, i) + ld(b, i));
+}
+
 int grid_for(int64_t work, int per_block, int cap) {
     int64_t b = (work + per_block - 1) / per_block;
     if (b > cap) b = cap;
@@ -460,6 +484,18 @@ cudaError_t gelu_bwd_t(cudaStream_t st, int sm_count, const T* g, const T* x, T*
 }
 
 template <typename T>
+cudaError_t add_t(cudaStream_t st, int sm_count, const T* a, const T* b, T* out, int64_t n) {
+    const bool vec = aligned16(a) && aligned16(b) && aligned16(out);
+    const int grid = grid_for(vec ? n / Vec<T>::N + 1 : n, 256, sm_count * 8);
+    if (vec)
+        add_kernel<T, true><<<grid, 256, 0, st>>>(a, b, out, n);
+    else
+        add_kernel<T, false><<<grid, 256, 0, st>>>(a, b, out, n);
+    note_launch();
+    return cudaGetLastError();
+}
+
+template <typename T>
 cudaError_t rows_init_t(cudaStream_t st, int sm_count, T* y, const T* res, const T* b, int64_t rows, int cols) {
     const bool vec = cols % Vec<T>::N == 0 && aligned16(y) && aligned16(res) && aligned16(b);
     const int ncv = vec ? cols / Vec<T>::N : cols;
@@ -507,6 +543,12 @@ cudaError_t gelu_bwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* g, 
     if (dt == HX_BF16)
         return gelu_bwd_t(st, sm_count, (const __nv_bfloat16*)g, (const __nv_bfloat16*)x, (__nv_bfloat16*)dx, n);
     return gelu_bwd_t(st, sm_count, (const float*)g, (const float*)x, (float*)dx, n);
+}
+
+cudaError_t add(cudaStream_t st, int sm_count, hx_dtype dt, const void* a, const void* b, void* out, int64_t n) {
+    if (dt == HX_BF16)
+        return add_t(st, sm_count, (const __nv_bfloat16*)a, (const __nv_bfloat16*)b, (__nv_bfloat16*)out, n);
+    return add_t(st, sm_count, (const float*)a, (const float*)b, (float*)out, n);
 }
 
 cudaError_t rows_init(cudaStream_t st, int sm_count, hx_dtype dt, void* y, const void* res, const void* b,

@@ -11,7 +11,12 @@
 //   Tensor::flash_attention <- src/tensor.rs:644-666
 //   FlashAttentionOp <- src/ops/flash_attention.rs (backward -> [dq, dk, dv])
 //   Op, Node, with_node, topo_sort, backward_with_seed
-//                    <- src/autograd.rs:55-118, src/tensor.rs:240-266
+//                    <- src/autograd.rs:55-118, src/tensor.rs:240-266 (gradients
+//                       that meet are summed with add, kernels/binary.rs:40)
+//   Linear, RMSNorm, MultiHeadAttention
+//                    <- src/nn/linear.rs, src/nn/rms_norm.rs, src/nn/attention.rs:46-98
+//                       (f32, the reference's GPU dtype; heads split and merged
+//                       as strided views of the projections, not copies)
 //
 // The reference panics on misuse (tensor.rs:652 "FlashAttention currently
 // requires GPU"); this layer throws haelixe::Error with the same text, and
@@ -162,6 +167,10 @@ class Tensor {
     Tensor flash_attention(const Tensor& k, const Tensor& v, float scale) const;
     Tensor flash_attention_causal(const Tensor& k, const Tensor& v, float scale) const;
 
+    // A tensor sharing this one's storage with another shape / strides (no copy;
+    // no autograd node: see ViewOp).
+    Tensor view(Shape shape, std::vector<int64_t> strides) const;
+
     Tensor with_node(std::shared_ptr<Op> op, std::vector<Tensor> parents) const;  // autograd.rs:68-78
     std::vector<Tensor> topo_sort() const;                                         // autograd.rs:82-110
     // Reverse-mode AD from a seed gradient (tensor.rs:240-266): every tensor of
@@ -193,6 +202,59 @@ class FlashAttentionOp : public Op {
           lse(std::move(lse_)), causal(causal_) {}
     const char* name() const override { return "FlashAttention"; }
     std::vector<std::optional<Tensor>> backward(const Tensor& grad_out) const override;
+};
+
+// Element-wise a + b of same-shape, same-layout tensors on one device
+// (kernels/binary.rs:40-60 without broadcasting).
+Tensor add(const Tensor& a, const Tensor& b);
+
+// A reinterpretation of the parent's storage (shape / strides change, no
+// data moves): the backward hands the gradient back with the parent's shape
+// and strides, which needs the gradient in the view's memory layout.
+class ViewOp : public Op {
+  public:
+    Shape src_shape;
+    std::vector<int64_t> src_strides, view_strides;
+    ViewOp(Shape s, std::vector<int64_t> ss, std::vector<int64_t> vs)
+        : src_shape(std::move(s)), src_strides(std::move(ss)), view_strides(std::move(vs)) {}
+    const char* name() const override { return "View"; }
+    std::vector<std::optional<Tensor>> backward(const Tensor& grad_out) const override;
+};
+
+// ---- nn (src/nn) ---------------------------------------------------------------
+
+// src/nn/linear.rs:54-56: y = x w + b with w stored [in, out].
+class Linear {
+  public:
+    Tensor weight, bias;
+    Linear(size_t in_features, size_t out_features, const Device& device, uint64_t seed);
+    Tensor forward(const Tensor& x) const;
+};
+
+// src/nn/rms_norm.rs: weight initialised to ones, eps 1e-5.
+class RMSNorm {
+  public:
+    Tensor weight;
+    float eps = 1e-5f;
+    RMSNorm(size_t hidden, const Device& device);
+    Tensor forward(const Tensor& x) const;
+};
+
+// src/nn/attention.rs:5-98: pre-RMSNorm, Q/K/V projections, heads as strided
+// views, RoPE (base 10000, attention.rs:76) on Q and K, the fused attention
+// with scale 1/sqrt(head_dim), heads merged by a view, output projection.
+// `causal` adds the mask the reference's layer lacks (false reproduces it).
+class MultiHeadAttention {
+  public:
+    RMSNorm norm;
+    Linear q_proj, k_proj, v_proj, out_proj;
+    size_t num_heads, head_dim;
+    bool causal;
+    float rope_base = 10000.0f;
+    MultiHeadAttention(size_t hidden, size_t num_heads, const Device& device, bool causal = false,
+                       uint64_t seed = 0);
+    Tensor forward(const Tensor& x) const;  // x: [B, S, hidden]
+    std::vector<Tensor*> parameters();
 };
 
 // Moves a tensor across devices in the graph (the ContiguousOp node that

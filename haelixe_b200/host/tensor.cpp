@@ -240,6 +240,43 @@ std::vector<std::optional<Tensor>> ToDeviceOp::backward(const Tensor& grad_out) 
     return {grad_out.to(source)};
 }
 
+Tensor Tensor::view(Shape new_shape, std::vector<int64_t> new_strides) const {
+    if (new_strides.size() != new_shape.dims().size()) throw Error("view: one stride per dimension");
+    Tensor t = *this;
+    t.id = TensorId::next();
+    t.shape = std::move(new_shape);
+    t.strides = std::move(new_strides);
+    t.requires_grad = false;
+    t.node = nullptr;
+    return t;
+}
+
+Tensor add(const Tensor& a, const Tensor& b) {
+    if (a.device != b.device || a.dtype != b.dtype || !(a.shape == b.shape) || a.strides != b.strides)
+        throw Error("add: operands must share device, dtype, shape and strides");
+    const size_t n = a.shape.num_elements();
+    // Dense layouts only (contiguous, or a permutation of a contiguous block):
+    // the element order then is the same in a, b and the result.
+    Tensor out = Tensor::empty(a.dtype, a.shape, a.device).view(a.shape, a.strides);
+    if (a.device.is_cuda()) {
+        hx_ctx* c = a.device.context()->raw();
+        check(c, hx_add(c, code_of(a.dtype), a.data_ptr(), b.data_ptr(), out.data_ptr_mut(), n));
+    } else {
+        if (a.dtype != DType::F32) throw Error("add: CPU tensors are f32 on this path");
+        const float* x = static_cast<const float*>(a.data_ptr());
+        const float* y = static_cast<const float*>(b.data_ptr());
+        float* z = static_cast<float*>(out.data_ptr_mut());
+        for (size_t i = 0; i < n; ++i) z[i] = x[i] + y[i];
+    }
+    return out;
+}
+
+std::vector<std::optional<Tensor>> ViewOp::backward(const Tensor& grad_out) const {
+    if (grad_out.strides != view_strides)
+        throw Error("View backward: the gradient is not in the view's memory layout");
+    return {grad_out.view(src_shape, src_strides)};
+}
+
 // ---- autograd ----------------------------------------------------------------------
 
 Tensor Tensor::with_node(std::shared_ptr<Op> op, std::vector<Tensor> parents) const {
@@ -285,9 +322,11 @@ std::unordered_map<uint64_t, Tensor> Tensor::backward_with_seed(const Tensor& se
         for (size_t i = 0; i < t.node->parents.size() && i < pg.size(); ++i) {
             if (!pg[i]) continue;
             const uint64_t pid = t.node->parents[i].id.value;
-            if (grads.count(pid))  // kernels::add in the reference; no graph of this path reuses a tensor
-                throw Error("backward_with_seed: gradient accumulation is not part of the attention path");
-            grads.emplace(pid, *pg[i]);
+            auto have = grads.find(pid);
+            if (have == grads.end())
+                grads.emplace(pid, *pg[i]);
+            else  // a tensor used more than once: gradients sum (tensor.rs:211-214)
+                have->second = add(have->second, *pg[i]);
         }
     }
     return grads;

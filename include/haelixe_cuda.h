@@ -31,6 +31,8 @@
  *                                        and the matmul/add backward it records
  *   hx_rmsnorm_fwd / hx_rmsnorm_bwd   <- rms_norm_forward / rms_norm_backward
  *                                        (src/kernels/rms_norm.rs:20-132)
+ *   hx_add                            <- kernels::add (src/kernels/binary.rs:40), the
+ *                                        autograd walk's gradient accumulation
  *   hx_gelu_fwd / hx_gelu_bwd         <- gelu / gelu_backward
  *                                        (src/kernels/activations.rs:192-237)
  *   hx_linear_residual_fwd            <- Linear::forward followed by the residual
@@ -232,6 +234,11 @@ int hx_rmsnorm_fwd(hx_ctx* ctx, hx_dtype dtype, const void* x, const void* w, vo
  * over the rows. */
 int hx_rmsnorm_bwd(hx_ctx* ctx, hx_dtype dtype, const void* dy, const void* x, const void* w, void* dx,
                    float* dw, int rows, int hidden, float eps);
+
+/* out = a + b over n elements (src/kernels/binary.rs:40-60 for equal shapes): the
+ * gradient accumulation of the autograd walk (src/tensor.rs:211-214); out may
+ * alias a or b. */
+int hx_add(hx_ctx* ctx, hx_dtype dtype, const void* a, const void* b, void* out, uint64_t n);
 
 /* GELU, tanh form, element-wise over n elements (src/kernels/activations.rs:192-209),
  * used by FeedForward (src/nn/mlp.rs); x and y may alias. */

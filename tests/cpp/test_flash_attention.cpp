@@ -24,6 +24,12 @@ int ora_attn_fwd(const float* q, const float* k, const float* v, float* o, float
 int ora_attn_bwd(const float* q, const float* k, const float* v, const float* dout, float* dq, float* dk,
                  float* dv, int BH, int S, int D, float scale, int causal, int ref_compat);
 void ora_round_bf16(const float* x, float* y, long n);
+void ora_matmul(const float* a, const float* b, float* out, long m, long k, long n);
+void ora_rms_norm_fwd(const float* x, const float* w, float* out, long rows, int hidden, float eps);
+void ora_rms_norm_bwd(const float* g, const float* x, const float* w, float* dx, float* dw, long rows, int hidden,
+                      float eps);
+void ora_rope_fwd(const float* x, float* out, long tokens, int S, int D, float base);
+void ora_rope_bwd(const float* g, float* out, long tokens, int S, int D, float base);
 }
 
 using haelixe::Device;
@@ -138,7 +144,7 @@ void attention_case(DType dt, int BH, int S, int D, bool causal, float tol) {
     assert_tensor_eq(grads.at(vt.id.value).to_vec_f32(), rdv, tol, "dV");
 }
 
-// max-abs 1e-3 for f32 I/O, 2e-2 for bf16 I/O.
+// The path's parity tolerances: max-abs 1e-3 for f32 I/O, 2e-2 for bf16 I/O.
 void test_flash_attention_f32_matches_oracle() { attention_case(DType::F32, 2, 80, 64, false, 1e-3f); }
 void test_flash_attention_f32_causal_matches_oracle() { attention_case(DType::F32, 3, 77, 32, true, 1e-3f); }
 void test_flash_attention_bf16_causal_matches_oracle() { attention_case(DType::BF16, 2, 320, 128, true, 2e-2f); }
@@ -185,6 +191,154 @@ void test_gradient_through_to() {  // tests/tensor_tests.rs:105-115
     }
 }
 
+// ---- the attention layer (nn/attention.rs:46-98) -----------------------------------
+
+using Vec = std::vector<float>;
+
+Vec transpose(const Vec& a, size_t rows, size_t cols) {
+    Vec t(a.size());
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t c = 0; c < cols; ++c) t[c * rows + r] = a[r * cols + c];
+    return t;
+}
+
+Vec matmul(const Vec& a, const Vec& b, size_t m, size_t k, size_t n) {
+    Vec out(m * n);
+    ora_matmul(a.data(), b.data(), out.data(), (long)m, (long)k, (long)n);
+    return out;
+}
+
+Vec col_sum(const Vec& a, size_t rows, size_t cols) {
+    Vec s(cols, 0.f);
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t c = 0; c < cols; ++c) s[c] += a[r * cols + c];
+    return s;
+}
+
+struct MhaParams {
+    Vec norm_w, w[4], b[4];  // q, k, v, o; weights [in, out]
+};
+
+struct MhaGrads {
+    Vec y, dx, norm_w, w[4], b[4];
+};
+
+// MultiHeadAttention::forward and its backward composed from the oracle's
+// kernels, in the reference's op order (the C restatement of oracle.py's
+// mha_forward / mha_backward).
+MhaGrads mha_oracle(const Vec& x, const MhaParams& p, const Vec& dy, size_t B, size_t S, size_t H, size_t D,
+                    bool causal) {
+    const size_t Hd = H * D, rows = B * S;
+    const float scale = 1.0f / std::sqrt((float)D), eps = 1e-5f, base = 10000.0f;
+    auto split = [&](const Vec& t) {  // [B, S, H*D] -> [B*H, S, D]
+        Vec o(t.size());
+        for (size_t b = 0; b < B; ++b)
+            for (size_t s = 0; s < S; ++s)
+                for (size_t h = 0; h < H; ++h)
+                    for (size_t d = 0; d < D; ++d) o[((b * H + h) * S + s) * D + d] = t[(b * S + s) * Hd + h * D + d];
+        return o;
+    };
+    auto merge = [&](const Vec& t) {  // the inverse
+        Vec o(t.size());
+        for (size_t b = 0; b < B; ++b)
+            for (size_t s = 0; s < S; ++s)
+                for (size_t h = 0; h < H; ++h)
+                    for (size_t d = 0; d < D; ++d) o[(b * S + s) * Hd + h * D + d] = t[((b * H + h) * S + s) * D + d];
+        return o;
+    };
+    auto rope = [&](const Vec& t, bool fwd) {
+        Vec o(t.size());
+        (fwd ? ora_rope_fwd : ora_rope_bwd)(t.data(), o.data(), (long)(B * H * S), (int)S, (int)D, base);
+        return o;
+    };
+    MhaGrads g;
+    Vec n(rows * Hd);
+    ora_rms_norm_fwd(x.data(), p.norm_w.data(), n.data(), (long)rows, (int)Hd, eps);
+    Vec proj[3];
+    for (int c = 0; c < 3; ++c) {
+        proj[c] = matmul(n, p.w[c], rows, Hd, Hd);
+        for (size_t r = 0; r < rows; ++r)
+            for (size_t j = 0; j < Hd; ++j) proj[c][r * Hd + j] += p.b[c][j];
+    }
+    const Vec qr = rope(split(proj[0]), true), kr = rope(split(proj[1]), true), vs = split(proj[2]);
+    Vec o(qr.size());
+    ora_attn_fwd(qr.data(), kr.data(), vs.data(), o.data(), nullptr, (int)(B * H), (int)S, (int)D, scale, causal);
+    const Vec om = merge(o);
+    g.y = matmul(om, p.w[3], rows, Hd, Hd);
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t j = 0; j < Hd; ++j) g.y[r * Hd + j] += p.b[3][j];
+    g.w[3] = matmul(transpose(om, rows, Hd), dy, Hd, rows, Hd);
+    g.b[3] = col_sum(dy, rows, Hd);
+    const Vec dout = split(matmul(dy, transpose(p.w[3], Hd, Hd), rows, Hd, Hd));
+    Vec dq(qr.size()), dk(qr.size()), dv(qr.size());
+    ora_attn_bwd(qr.data(), kr.data(), vs.data(), dout.data(), dq.data(), dk.data(), dv.data(), (int)(B * H), (int)S,
+                 (int)D, scale, causal, 0);
+    const Vec dproj[3] = {merge(rope(dq, false)), merge(rope(dk, false)), merge(dv)};
+    Vec dn(rows * Hd, 0.f);
+    for (int c = 0; c < 3; ++c) {
+        g.w[c] = matmul(transpose(n, rows, Hd), dproj[c], Hd, rows, Hd);
+        g.b[c] = col_sum(dproj[c], rows, Hd);
+        const Vec t = matmul(dproj[c], transpose(p.w[c], Hd, Hd), rows, Hd, Hd);
+        for (size_t i = 0; i < dn.size(); ++i) dn[i] += t[i];
+    }
+    g.dx.resize(rows * Hd);
+    g.norm_w.resize(Hd);
+    ora_rms_norm_bwd(dn.data(), x.data(), p.norm_w.data(), g.dx.data(), g.norm_w.data(), (long)rows, (int)Hd, eps);
+    return g;
+}
+
+void mha_case(bool causal) {
+    const size_t B = 2, S = 128, H = 4, D = 64, Hd = H * D;  // the reference's CPU-runnable layer shape
+    std::mt19937 gen(99);
+    std::uniform_real_distribution<float> uw(-std::sqrt(6.0f / Hd), std::sqrt(6.0f / Hd)), ub(-0.1f, 0.1f),
+        un(0.5f, 1.5f);
+    MhaParams p;
+    p.norm_w.resize(Hd);
+    for (auto& v : p.norm_w) v = un(gen);
+    for (int c = 0; c < 4; ++c) {
+        p.w[c].resize(Hd * Hd);
+        p.b[c].resize(Hd);
+        for (auto& v : p.w[c]) v = uw(gen);
+        for (auto& v : p.b[c]) v = ub(gen);
+    }
+    const Vec x = randn(B * S * Hd, 31, false), dy = randn(B * S * Hd, 32, false);
+    const Device cuda = Device::cuda();
+    haelixe::MultiHeadAttention mha(Hd, H, cuda, causal);
+    auto param = [&](const Vec& v, Shape s) { return Tensor::from_slice(DType::F32, s, v).to(cuda).requires_grad_(true); };
+    mha.norm.weight = param(p.norm_w, Shape{Hd});
+    haelixe::Linear* lin[4] = {&mha.q_proj, &mha.k_proj, &mha.v_proj, &mha.out_proj};
+    for (int c = 0; c < 4; ++c) {
+        lin[c]->weight = param(p.w[c], Shape{Hd, Hd});
+        lin[c]->bias = param(p.b[c], Shape{Hd});
+    }
+    const Tensor xt = param(x, Shape{B, S, Hd});
+    const Tensor y = mha.forward(xt);
+    const auto grads = y.backward_with_seed(Tensor::from_slice(DType::F32, Shape{B, S, Hd}, dy).to(cuda));
+    const MhaGrads r = mha_oracle(x, p, dy, B, S, H, D, causal);
+    const float tol = 1e-3f;  // f32 I/O
+    assert_tensor_eq(y.to_vec_f32(), r.y, tol, "y");
+    assert_tensor_eq(grads.at(xt.id.value).to_vec_f32(), r.dx, tol, "dx");
+    assert_tensor_eq(grads.at(mha.norm.weight.id.value).to_vec_f32(), r.norm_w, tol, "d norm_w");
+    const char* names[4] = {"q", "k", "v", "o"};
+    for (int c = 0; c < 4; ++c) {
+        assert_tensor_eq(grads.at(lin[c]->weight.id.value).to_vec_f32(), r.w[c], tol, std::string("d w") + names[c]);
+        assert_tensor_eq(grads.at(lin[c]->bias.id.value).to_vec_f32(), r.b[c], tol, std::string("d b") + names[c]);
+    }
+}
+
+void test_multi_head_attention_matches_oracle() { mha_case(false); }
+void test_multi_head_attention_causal_matches_oracle() { mha_case(true); }
+
+void test_multi_head_attention_rejects_bad_heads() {  // attention.rs:24-28
+    try {
+        haelixe::MultiHeadAttention bad(10, 3, Device::cpu());
+    } catch (const haelixe::Error& e) {
+        require(std::string(e.what()).find("divisible") != std::string::npos, e.what());
+        return;
+    }
+    throw Failure{"hidden_dim % num_heads != 0 must be refused"};
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -206,6 +360,9 @@ int main(int argc, char** argv) {
         {"to_roundtrip_is_exact", test_to_roundtrip_is_exact, true},
         {"arena_slab_returns_on_last_drop", test_arena_slab_returns_on_last_drop, true},
         {"gradient_through_to", test_gradient_through_to, true},
+        {"multi_head_attention_matches_oracle", test_multi_head_attention_matches_oracle, true},
+        {"multi_head_attention_causal_matches_oracle", test_multi_head_attention_causal_matches_oracle, true},
+        {"multi_head_attention_rejects_bad_heads", test_multi_head_attention_rejects_bad_heads, false},
     };
     int failed = 0, ran = 0;
     for (const auto& c : cases) {

@@ -35,7 +35,7 @@ def _run(*args):
 
 def test_host_layer_cpu_cases():
     out = _run("--cpu-only")
-    assert "4 of 4 passed" in out
+    assert "5 of 5 passed" in out
 
 
 def test_host_library_exports_the_mirror():
@@ -53,4 +53,4 @@ def test_host_library_exports_the_mirror():
 @pytest.mark.gpu
 def test_host_layer_on_gpu():
     out = _run()
-    assert "11 of 11 passed" in out
+    assert "14 of 14 passed" in out
