@@ -76,8 +76,9 @@ extern "C" int hx_flash_attention_bwd_noalloc(hx_ctx* c, hx_dtype dt, const void
         return set_error(c, HX_ERR_UNSUPPORTED,
                          "%s: only bf16 with head_dim 64 or 128 (the tcgen05 kernels) is supported",
                          who);
-    if (bh <= 0 || seq_len <= 0 || bh > 65535)
+    if (bh < 0 || seq_len < 0 || bh > 65535)
         return set_error(c, HX_ERR_INVALID, "%s: bad shape bh=%d seq_len=%d", who, bh, seq_len);
+    if (bh == 0 || seq_len == 0) return HX_OK;  // empty problem
     if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv)
         return set_error(c, HX_ERR_INVALID, "%s: NULL operand", who);
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(dout) ||

@@ -75,11 +75,14 @@ struct DeviceGuard {
     }
 };
 
+// B, H or S may be 0 (an empty problem: nothing to compute, see empty_shape);
+// D must be positive.
 int validate_shape(const hx_ctx* ctx, const hx_attn_shape* s, const char* who) {
     if (s == nullptr) return set_error(ctx, HX_ERR_INVALID, "%s: shape is NULL", who);
-    if (s->B <= 0 || s->H <= 0 || s->S <= 0 || s->D <= 0)
-        return set_error(ctx, HX_ERR_INVALID, "%s: B, H, S, D must be positive (got %d,%d,%d,%d)",
-                         who, s->B, s->H, s->S, s->D);
+    if (s->B < 0 || s->H < 0 || s->S < 0 || s->D <= 0)
+        return set_error(ctx, HX_ERR_INVALID,
+                         "%s: B, H, S must be >= 0 and D positive (got %d,%d,%d,%d)", who, s->B, s->H,
+                         s->S, s->D);
     if (s->D > 256)
         return set_error(ctx, HX_ERR_UNSUPPORTED, "%s: head_dim %d > 256 is not supported", who,
                          s->D);
@@ -92,6 +95,11 @@ int validate_shape(const hx_ctx* ctx, const hx_attn_shape* s, const char* who) {
                          s->D);
     return HX_OK;
 }
+
+// No rows to attend over: every entry point returns HX_OK without touching
+// its operands (which may then be NULL), as an empty tensor in gives an
+// empty tensor out.
+inline bool empty_shape(const hx_attn_shape* s) { return s->B == 0 || s->H == 0 || s->S == 0; }
 
 int validate_dtype(const hx_ctx* ctx, hx_dtype dt, const char* who) {
     if (dt != HX_F32 && dt != HX_BF16)
@@ -405,6 +413,7 @@ int hx_attn_fwd_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, cons
     int st;
     if ((st = validate_dtype(c, dt, "hx_attn_fwd")) || (st = validate_shape(c, shape, "hx_attn_fwd")))
         return st;
+    if (empty_shape(shape)) return HX_OK;
     if (!q || !k || !v || !o) return set_error(c, HX_ERR_INVALID, "hx_attn_fwd: NULL operand");
     if (!isfinite(scale)) return set_error(c, HX_ERR_INVALID, "hx_attn_fwd: scale is not finite");
     DeviceGuard g(c->device);
@@ -428,6 +437,10 @@ int hx_attn_fwd_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, cons
 int hx_attn_bwd_workspace_size(hx_dtype dt, const hx_attn_shape* shape, uint64_t* bytes) {
     if (shape == nullptr || bytes == nullptr) return HX_ERR_INVALID;
     if (validate_dtype(nullptr, dt, "") || validate_shape(nullptr, shape, "")) return HX_ERR_INVALID;
+    if (empty_shape(shape)) {
+        *bytes = 0;
+        return HX_OK;
+    }
     const hx::AttnDims d = hx::dims_of(*shape);
     uint64_t n = simt_ws_bytes(d);
     if (hx::sm100_bwd_supported(dt, d)) n = std::max(n, hx::sm100_bwd_workspace_bytes(d));
@@ -466,6 +479,7 @@ static int attn_bwd_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, c
     int st;
     if ((st = validate_dtype(c, dt, "hx_attn_bwd")) || (st = validate_shape(c, shape, "hx_attn_bwd")))
         return st;
+    if (empty_shape(shape)) return HX_OK;
     float2* tab = nullptr;
     if (rope_base != nullptr) {
         if (shape->D % 2) return set_error(c, HX_ERR_INVALID, "hx_attn_bwd_rope: head_dim must be even");
@@ -589,6 +603,7 @@ static int rope_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const
     if (c == nullptr) return HX_ERR_INVALID;
     int st;
     if ((st = validate_dtype(c, dt, who)) || (st = validate_shape(c, shape, who))) return st;
+    if (empty_shape(shape)) return HX_OK;
     if (!x || !out) return set_error(c, HX_ERR_INVALID, "%s: NULL operand", who);
     if (shape->D % 2) return set_error(c, HX_ERR_INVALID, "%s: head_dim must be even", who);
     if (!isfinite(base) || base <= 0.f)

@@ -86,7 +86,10 @@ typedef enum hx_status {
 /* Shape and element strides of one attention operand viewed as [B, H, S, D]
  * with D contiguous. q, k, v, o, dO, dQ, dK and dV of one call share it.
  * The reference's contiguous [B*H, S, D] tensors are B = B*H, H = 1,
- * stride_s = D, stride_b = S*D (what hx_flash_attention_* pass). */
+ * stride_s = D, stride_b = S*D (what hx_flash_attention_* pass).
+ * B, H or S of 0 is an empty problem: the attention and RoPE calls return
+ * HX_OK without touching their operands (which may be NULL); D must be
+ * positive. */
 typedef struct hx_attn_shape {
     int32_t B, H, S, D;
     int64_t stride_b, stride_h, stride_s;

@@ -6,6 +6,7 @@ bf16-rounded inputs. bf16 outputs are rounded to bf16, whose spacing exceeds
 2e-2 above magnitude 4; for such elements the bound is widened to one bf16
 spacing of the oracle value (`_bf16_tol`).
 """
+import ctypes
 import math
 
 import numpy as np
@@ -329,3 +330,19 @@ def test_ragged_lengths_tcgen05():
     """Sequence lengths that leave partial K/V and query tiles at the end."""
     for S, D in ((1000, 128), (2049, 64), (1537, 128)):
         _sampled_full_size(1, 2, S, D, True, samples=((0, 1),))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("shape", [(0, 64, 64), (3, 0, 128), (0, 4, 16, 64), (2, 0, 16, 64)])
+def test_empty_inputs_give_empty_outputs(dtype, shape):
+    """An empty batch, head count or sequence is a no-op: empty outputs and
+    gradients, no error (the attention and RoPE entry points return HX_OK)."""
+    q, k, v = (torch.zeros(shape, device="cuda", dtype=dtype).requires_grad_() for _ in range(3))
+    o = hx.flash_attention(q, k, v, 0.125, causal=True, rope_base=10000.0)
+    assert o.shape == q.shape and o.numel() == 0
+    o.backward(torch.zeros_like(o))
+    assert all(t.grad is not None and t.grad.shape == q.shape for t in (q, k, v))
+    ws = ctypes.c_uint64(1)
+    N.check(N.lib().hx_attn_bwd_workspace_size(N.HX_BF16, ctypes.byref(hx.attention._shape_of(q.detach())),
+                                               ctypes.byref(ws)))
+    assert ws.value == 0
