@@ -505,7 +505,9 @@ cudaError_t launch(cudaStream_t st, DeviceStatus* status, const AttnDims& d, con
     prm.causal = causal;
     prm.hgroup = HX_FWD_HGROUP;
     prm.status = status;
-    dim3 grid((unsigned)((d.S + NWG * BM - 1) / (NWG * BM) * d.H * d.B));
+    const int64_t blocks = (int64_t)((d.S + NWG * BM - 1) / (NWG * BM)) * d.H * d.B;
+    if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;  // past the grid's x limit
+    dim3 grid((unsigned)blocks);
     attn_fwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, prm);
     note_launch();
     return cudaGetLastError();
