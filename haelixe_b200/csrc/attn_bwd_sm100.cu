@@ -811,9 +811,9 @@ cudaError_t launch(cudaStream_t st, int sm_count, DeviceStatus* status, const At
     prm.rope_tab = rope_tab;
     prm.hgroup = HX_BWD_HGROUP;
     prm.status = status;
-    const int64_t blocks = (int64_t)((d.S + BK - 1) / BK) * d.H * d.B;
-    if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;  // past the grid's x limit
-    dim3 grid((unsigned)blocks);
+    const int64_t main_blocks = (int64_t)((d.S + BK - 1) / BK) * d.H * d.B;
+    if (main_blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;  // past the grid's x limit
+    dim3 grid((unsigned)main_blocks);
     attn_bwd_kernel<D><<<grid, kThreads, C::SMEM, st>>>(tq, tk, tv, tdo, tdq, prm);
     note_launch();
     e = cudaGetLastError();
