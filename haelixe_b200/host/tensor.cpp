@@ -86,13 +86,15 @@ hx_arena_stats CudaContext::arena_stats() const {
 }
 
 std::shared_ptr<CudaContext> CudaContext::get(int device) {
+    // Process-lifetime contexts, deliberately never destroyed: a static map's
+    // destructor would run at exit after the CUDA runtime's own teardown.
     static std::mutex mu;
-    static std::unordered_map<int, std::shared_ptr<CudaContext>> contexts;
+    static auto* contexts = new std::unordered_map<int, std::shared_ptr<CudaContext>>();
     std::lock_guard<std::mutex> lk(mu);
-    auto it = contexts.find(device);
-    if (it != contexts.end()) return it->second;
+    auto it = contexts->find(device);
+    if (it != contexts->end()) return it->second;
     auto c = std::make_shared<CudaContext>(device);
-    contexts[device] = c;
+    (*contexts)[device] = c;
     return c;
 }
 
