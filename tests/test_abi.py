@@ -74,3 +74,15 @@ def test_workspace_size():
     assert out.value >= 2 * 3 * 100 * 4 and out.value % 256 == 0
     bad = N.AttnShape(2, 3, 100, 0, 0, 0, 0)
     assert L.hx_attn_bwd_workspace_size(N.HX_F32, ctypes.byref(bad), ctypes.byref(out)) == N.HX_ERR_INVALID
+
+
+def test_rust_binding_declares_every_entry_point():
+    """INTEGRATION.md's `extern "C"` block binds every function the header declares."""
+    import re
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    header = open(os.path.join(root, "include", "haelixe_cuda.h")).read()
+    declared = set(re.findall(r"^\s*(?:int|uint64_t|const char\*|void\*)\s+(hx_\w+)\s*\(", header, re.M))
+    binding = open(os.path.join(root, "INTEGRATION.md")).read()
+    bound = set(re.findall(r"pub fn (hx_\w+)\(", binding))
+    assert declared and not (declared - bound), sorted(declared - bound)
