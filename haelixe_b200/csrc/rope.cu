@@ -39,22 +39,32 @@ __device__ __forceinline__ void rot(float x0, float x1, float2 cs, float sign, f
     y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs.x));
 }
 
+// x / 2^k and x % 2^k when k >= 0 (a power-of-two divisor), else plain
+// division: the row index splits into (b, h, s, group) without integer
+// divides for the usual power-of-two S, H and D.
+template <typename I>
+__device__ __forceinline__ I div_by(I x, I v, int k) { return k >= 0 ? (x >> k) : x / v; }
+template <typename I>
+__device__ __forceinline__ I mod_by(I x, I v, int k) { return k >= 0 ? (x & (v - 1)) : x % v; }
+
 // One thread per 4 pairs (8 elements) of a row; rows are [.., S, D] with
-// element strides; D % 8 == 0 on this path.
-template <typename T>
+// element strides; D % 8 == 0 on this path. I is the index type: 32-bit
+// when the host has checked that the index space and one grid stride fit,
+// else 64-bit. gk, sk, hk: log2 of D/8, S, H, or -1 when not a power of two.
+template <typename T, typename I>
 __global__ void __launch_bounds__(256) rope_kernel8(const T* x, T* out, const float2* __restrict__ tab,
-                                                    AttnDims d, float sign) {
+                                                    AttnDims d, float sign, int gk, int sk, int hk) {
     const int half = d.D / 2;
-    const int groups = d.D / 8;
-    const int64_t total = (int64_t)d.B * d.H * d.S * groups;
-    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (int64_t)gridDim.x * blockDim.x) {
-        const int g = (int)(idx % groups);
-        int64_t r = idx / groups;
-        const int s = (int)(r % d.S);
-        r /= d.S;
-        const int h = (int)(r % d.H);
-        const int b = (int)(r / d.H);
+    const I groups = (I)(d.D / 8), S = (I)d.S, H = (I)d.H;
+    const I total = (I)d.B * H * S * groups;
+    const I stride = (I)gridDim.x * (I)blockDim.x;
+    for (I idx = (I)blockIdx.x * (I)blockDim.x + (I)threadIdx.x; idx < total; idx += stride) {
+        const int g = (int)mod_by(idx, groups, gk);
+        I r = div_by(idx, groups, gk);
+        const int s = (int)mod_by(r, S, sk);
+        r = div_by(r, S, sk);
+        const int h = (int)mod_by(r, H, hk);
+        const int b = (int)div_by(r, H, hk);
         const int64_t off = (int64_t)b * d.sb + (int64_t)h * d.sh + (int64_t)s * d.ss + 8 * g;
         const float4* t4 = reinterpret_cast<const float4*>(tab + (int64_t)s * half + 4 * g);
         const float4 c01 = t4[0], c23 = t4[1];
@@ -136,8 +146,13 @@ cudaError_t launch_rope(cudaStream_t st, int sm_count, const AttnDims& d, const 
     const int64_t cap = (int64_t)sm_count * 16;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    if (vec)
-        rope_kernel8<T><<<(unsigned)blocks, 256, 0, st>>>((const T*)x, (T*)out, tab, d, sign);
+    auto log2_of = [](int64_t v) { return (v > 0 && (v & (v - 1)) == 0) ? __builtin_ctzll((uint64_t)v) : -1; };
+    const int gk = log2_of(d.D / 8), sk = log2_of(d.S), hk = log2_of(d.H);
+    if (vec && work + blocks * 256 < (int64_t(1) << 32))
+        rope_kernel8<T, uint32_t><<<(unsigned)blocks, 256, 0, st>>>((const T*)x, (T*)out, tab, d, sign, gk, sk,
+                                                                  hk);
+    else if (vec)
+        rope_kernel8<T, int64_t><<<(unsigned)blocks, 256, 0, st>>>((const T*)x, (T*)out, tab, d, sign, gk, sk, hk);
     else
         rope_kernel1<T><<<(unsigned)blocks, 256, 0, st>>>((const T*)x, (T*)out, tab, d, sign);
     note_launch();
