@@ -1,8 +1,8 @@
 """ctypes binding of libhaelixe_cuda.so (the C ABI in include/haelixe_cuda.h).
 
 This is the Python counterpart of the `extern "C"` block a Rust build of
-haelixe declares. There is no fallback: if the library is
-missing, loading fails loudly.
+haelixe declares. There is no fallback: if the library is missing, loading
+fails loudly.
 """
 from __future__ import annotations
 

@@ -25,8 +25,13 @@
 //     kernels overlap on the GPU (different streams, or different host
 //     threads) race on the array and corrupt each other. Serialize them.
 //   * The first call on each device looks up the array's device address
-//     (cudaGetSymbolAddress, with that device current). Make that first
-//     call before any stream capture begins.
+//     (cudaGetSymbolAddress, with that device current) and keeps it for the
+//     life of the process. Make that first call before any stream capture
+//     begins, and do not use the entry point after cudaDeviceReset (or any
+//     other teardown of the device's primary context): the kept address
+//     belonged to the destroyed context.
+//   * It always runs the tcgen05 kernels: a context forced onto the SIMT
+//     path (hx_set_force_simt) gets HX_ERR_UNSUPPORTED.
 #include <mutex>
 
 #include "hx_internal.h"
@@ -81,6 +86,12 @@ extern "C" int hx_flash_attention_bwd_noalloc(hx_ctx* c, hx_dtype dt, const void
     if (bh == 0 || seq_len == 0) return HX_OK;  // empty problem
     if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv)
         return set_error(c, HX_ERR_INVALID, "%s: NULL operand", who);
+    if (!isfinite(scale)) return set_error(c, HX_ERR_INVALID, "%s: scale is not finite", who);
+    if (c->force_simt)
+        return set_error(c, HX_ERR_UNSUPPORTED,
+                         "%s: the context is forced onto the SIMT path; this entry point runs "
+                         "only the tcgen05 kernels",
+                         who);
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(dout) ||
         !aligned16(dq) || !aligned16(dk) || !aligned16(dv))
         return set_error(c, HX_ERR_INVALID, "%s: operands must be 16-byte aligned", who);

@@ -2,7 +2,7 @@
  * haelixe_cuda.h - C ABI of the B200 (sm_100a) fused attention library.
  *
  * This is the boundary that haelixe's Rust crate binds through `extern "C"`
- * (see INTEGRATION.md for the Rust declarations and the build.rs step).
+ * (a build.rs step compiles this library with nvcc and links it).
  * Plain pointers and sizes only: device pointers are raw CUDA device
  * addresses on the context's device, host pointers are ordinary host memory.
  *
@@ -181,8 +181,11 @@ int hx_flash_attention_bwd(hx_ctx* ctx, hx_dtype dtype, const void* q, const voi
  * allocate). bf16 with head_dim 64 or 128 only. Problems whose workspace
  * (hx_attn_bwd_workspace_size) exceeds 64 MiB return HX_ERR_INVALID. Calls
  * share the array: calls that overlap on the GPU race, so serialize them.
- * The first call on a device resolves the array's address; make it before
- * any stream capture. */
+ * The first call on a device resolves the array's address and keeps it; make
+ * it before any stream capture, and do not call this after cudaDeviceReset.
+ * A non-finite scale returns HX_ERR_INVALID. It ignores no setting silently:
+ * a context forced onto the SIMT path (hx_set_force_simt) returns
+ * HX_ERR_UNSUPPORTED. */
 int hx_flash_attention_bwd_noalloc(hx_ctx* ctx, hx_dtype dtype, const void* q, const void* k,
                                    const void* v, const void* o, const void* dout,
                                    const float* lse, void* dq, void* dk, void* dv, int bh,

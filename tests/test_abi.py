@@ -77,7 +77,7 @@ def test_workspace_size():
 
 
 def test_rust_binding_declares_every_entry_point():
-    """INTEGRATION.md's `extern "C"` block binds every function the header declares."""
+    """The Rust `extern "C"` block of the integration guide binds every function the header declares."""
     import re
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))

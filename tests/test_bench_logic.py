@@ -48,3 +48,13 @@ def test_config_names_the_workload_and_the_l2_rule():
     assert bench.config_of(a, 8)["parallelism"].startswith("heads/8 per GPU")
     small = bench.config_of(_args("--seq", "1024", "--heads", "2"), 1)
     assert "smaller than L2" in small["l2"]
+
+
+def test_peak_rule_burst_for_short_regions_sustained_for_long():
+    peaks = {"bf16_tflops": 1643.5, "bf16_tflops_sustained": 1348.1}
+    p, src = bench.choose_peak(peaks, 0.083)  # ten 8.3 ms steps
+    assert p == 1643.5 and "burst" in src
+    p, src = bench.choose_peak(peaks, 5.0)
+    assert p == 1348.1 and "sustained" in src
+    p, src = bench.choose_peak(None, 0.1)
+    assert p == bench.FALLBACK_PEAK_TFLOPS and "fallback" in src
