@@ -90,6 +90,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--workload", choices=["attention", "block_stack"], default="attention")
+    p.add_argument("--exchange-flags", type=int, default=0,
+                   help="hx_group flags of the N>1 exchange: 1 register, 2 symmetric window, 4 copy engines")
     return p.parse_args()
 
 
@@ -303,8 +305,13 @@ def run_haelixe(a):
         raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    group = None
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        # Control (barriers, max over ranks) over gloo on the host; the data
+        # path's only collective is the library's own NCCL group.
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        from haelixe_b200.sharding import HeadGroup
+        group = HeadGroup.bootstrap(local, flags=a.exchange_flags, timeout_ms=120000)
     B, H, S, D = a.batch, a.heads, a.seq, a.head_dim
     causal = not a.no_causal
     if H % world:
@@ -331,12 +338,14 @@ def run_haelixe(a):
                     lse=torch.empty(B * Hl * S, device=dev, dtype=torch.float32))
 
     bufs0 = buffers(q, k, v, do)
+    if world > 1:
+        # The forward writes O straight into this rank's slot of the group's
+        # gather buffer, so the all-gather runs in place.
+        gbuf = group.gather_buffer((B, Hl, S, D), torch.bfloat16)
+        bufs0["o"] = gbuf[rank]
+        merged = torch.empty(B, S, H, D, device=dev, dtype=torch.bfloat16)
     qr, kr, o, lse = bufs0["qr"], bufs0["kr"], bufs0["o"], bufs0["lse"]
     dv, dq0, dk0 = bufs0["dv"], bufs0["dq0"], bufs0["dk0"]
-    if world > 1:
-        gathered = torch.empty(world * B * Hl * S * D, device=dev, dtype=torch.bfloat16)
-        merged = torch.empty(B, S, H, D, device=dev, dtype=torch.bfloat16)
-        comm = torch.cuda.Stream(device=dev)
     stream = torch.cuda.current_stream(dev)
     ev = {}
 
@@ -356,18 +365,9 @@ def run_haelixe(a):
         if timed:
             ev["f1"][-1].record(stream)
         if world > 1:
-            done = torch.cuda.Event()
-            done.record(stream)
-            comm.wait_event(done)
-            with torch.cuda.stream(comm):
-                dist.all_gather_into_tensor(gathered, o.reshape(-1))
-                # The reassembly needs only the gather: it runs on the same side
-                # stream, beside the backward, instead of after it.
-                ctx.use_stream()
-                N.check(N.lib().hx_reassemble_heads(ctx.handle, N.HX_BF16, gathered.data_ptr(),
-                                                    merged.data_ptr(), world, B, Hl, S, D, 1),
-                        ctx.handle)
-            ctx.use_stream()
+            # NCCL all-gather + reassembly into [B, S, H, D] on the group's
+            # side stream, after the forward and beside the backward.
+            group.all_gather(o, merged, "bshd")
         # Backward with the rotary embedding's backward fused into the last
         # writes of dQ and dK: dq0, dk0 are the gradients of q, k before RoPE.
         hx.attn_backward(qr, kr, v, o, lse, do, scale, causal, dq=dq0, dk=dk0, dv=dv,
@@ -375,7 +375,7 @@ def run_haelixe(a):
         if timed:
             ev["b1"][-1].record(stream)
         if world > 1:
-            stream.wait_stream(comm)  # the step ends with O gathered and merged on every rank
+            group.wait()  # the step ends with O gathered and merged on every rank
 
     for _ in range(a.warmup):
         step()
@@ -384,11 +384,11 @@ def run_haelixe(a):
         # Untimed check of the gathered output: this rank's heads of `merged`
         # are its own O, and every rank holds the same merged tensor.
         own = torch.equal(merged[:, :, rank * Hl:(rank + 1) * Hl], o.transpose(1, 2))
-        cs = merged.float().sum(dtype=torch.float64).reshape(1)
+        cs = merged.float().sum(dtype=torch.float64).reshape(1).cpu()
         lo, hi = cs.clone(), cs.clone()
         dist.all_reduce(lo, op=dist.ReduceOp.MIN)
         dist.all_reduce(hi, op=dist.ReduceOp.MAX)
-        ok = torch.tensor([1 if (own and lo.item() == hi.item()) else 0], device=dev)
+        ok = torch.tensor([1 if (own and lo.item() == hi.item()) else 0])
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
         if ok.item() != 1:
             raise SystemExit(f"rank {rank}: gathered heads do not match (own slice {own})")
@@ -414,7 +414,7 @@ def run_haelixe(a):
     ms = t_start.elapsed_time(t_end) / a.steps
     fwd_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(ev["f0"], ev["f1"]))
     bwd_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(ev["f1"], ev["b1"]))
-    t = torch.tensor([ms, fwd_ms, bwd_ms], device=dev, dtype=torch.float64)
+    t = torch.tensor([ms, fwd_ms, bwd_ms], dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, fwd_ms, bwd_ms = t.tolist()
@@ -457,7 +457,9 @@ def run_haelixe(a):
         }
         print(json.dumps(out), flush=True)
     if world > 1:
+        torch.cuda.synchronize()
         dist.barrier()
+        group.close()
         dist.destroy_process_group()
     return 0
 
@@ -529,7 +531,7 @@ def e2e_measure(a, ctx, N, torch, dev, world, sets, step, total_flops):
     t1.record(s_out)
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1) / steps
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    t = torch.tensor([ms], dtype=torch.float64)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms = t.item()

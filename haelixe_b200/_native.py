@@ -22,6 +22,11 @@ HX_ERR_OOM = -4
 HX_ERR_TIMEOUT = -5
 HX_ERR_NCCL = -6
 
+HX_GROUP_ID_BYTES = 128
+HX_GROUP_REGISTER = 1
+HX_GROUP_SYMMETRIC = 2
+HX_GROUP_COPY_ENGINE = 4
+
 
 class HxError(RuntimeError):
     def __init__(self, status: int, message: str):
@@ -106,9 +111,23 @@ SIGNATURES = {
     "hx_rope_fwd": (_I, [_P, _I, _SHP, _P, _P, _F]),
     "hx_rope_bwd": (_I, [_P, _I, _SHP, _P, _P, _F]),
     "hx_reassemble_heads": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _I, _I]),
+    "hx_group_unique_id": (_I, [_P]),
+    "hx_group_create_rank": (_I, [_I, _I, _I, _P, _I, _I, ctypes.POINTER(_P)]),
+    "hx_group_create": (_I, [_I, ctypes.POINTER(_I), _I, _I, ctypes.POINTER(_P)]),
+    "hx_group_destroy": (_I, [_P]),
+    "hx_group_abort": (_I, [_P]),
+    "hx_group_set_timeout": (_I, [_P, _I]),
+    "hx_group_info": (_I, [_P, ctypes.POINTER(_I), ctypes.POINTER(_I), ctypes.POINTER(_I)]),
+    "hx_group_last_error": (_I, [_P, ctypes.c_char_p, _U64]),
+    "hx_group_gather_buffer": (_I, [_P, _I, _U64, ctypes.POINTER(_P)]),
+    "hx_allgather_heads": (_I, [_P, _I, _P, _I, _P, _P, _I, _I, _I, _I, _I]),
+    "hx_group_wait": (_I, [_P, _I, _P]),
+    "hx_group_sync": (_I, [_P, _I]),
     "hx_kernel_launches": (_U64, [_P]),
     "hx_last_path": (_I, [_P]),
     "hx_set_force_simt": (_I, [_P, _I]),
+    "hx_last_gemm_path": (_I, [_P]),
+    "hx_set_gemm_backend": (_I, [_P, _I]),
     "hx_selftest_wait_timeout": (_I, [_P]),
     "hx_arena_set_limit": (_I, [_P, _U64]),
 }

@@ -79,7 +79,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
                 if verbose or ptxas_info:
                     print(out)
     if force or jobs or _stale(LIB, objs):
-        cmd = [nvcc] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart", "-lcublas"]
+        cmd = [nvcc] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart", "-lcublas", "-ldl"]
         run(cmd)
     build_host(force)
     return LIB

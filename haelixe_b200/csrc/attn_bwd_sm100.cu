@@ -16,9 +16,10 @@
 //           dK  += dS^T Q     (SS UMMA, dS^T K-major from smem)
 //           dQ   = dS K       (SS UMMA from the smem dS tile; for D=128 as
 //                              dQ^T = K^T dS^T so M = D = 128)  -> TMEM
-//         a drain warpgroup moves each dQ tile TMEM -> registers -> an f32
-//         smem staging tile, and one thread adds it into the accumulator with
-//         a bulk tensor reduce-add while the tensor core moves on;
+//         a drain warpgroup moves each dQ tile TMEM -> registers and adds it
+//         into the f32 accumulator in L2 (D=128: red.global.add from the
+//         registers; D=64: through an smem staging tile and a bulk tensor
+//         reduce-add) while the tensor core moves on;
 //   post  dQ = bf16(scale * accumulator), dK already carries the scale.
 // The scale on dQ and dK is the factor the reference's backward omits
 // (flash_attention.rs:31,34-36).
@@ -30,6 +31,7 @@
 // each query tile's columns (thread = key row = TMEM lane), warps 12-15 the
 // dQ drain warpgroup. All mbarrier waits are bounded (sm100_ptx.cuh).
 #include <math.h>
+#include <string.h>
 
 #include "sm100_ptx.cuh"
 #include "tma_host.h"
@@ -51,7 +53,9 @@ template <int D>
 struct BCfg {
     static constexpr int BQ = D == 128 ? 64 : 128;  // queries per inner tile
     static constexpr bool DQ_T = D == 128;           // dQ computed transposed (M = D)
-    static constexpr int QST = 2;                    // Q/dO/lse/delta ring depth
+    // Q/dO/lse/delta ring depth. D=128 uses the 64 KB the register dQ drain
+    // freed for a third stage (backward 6.32 -> 6.01 ms on C3).
+    static constexpr int QST = D == 128 ? 3 : 2;
     static constexpr int REGS_CTL = D == 128 ? 104 : 64;
     static constexpr int REGS_COMPUTE = D == 128 ? 160 : 168;
     static constexpr int REGS_DRAIN = D == 128 ? 88 : 112;
@@ -71,11 +75,18 @@ struct BCfg {
     static constexpr int Q_OFF = V_OFF + KT;
     static constexpr int DO_OFF = Q_OFF + QST * QT;
     static constexpr int DS_OFF = DO_OFF + QST * QT;
+    // dQ drain. D=128: red.global.add straight from the registers loaded from
+    // TMEM (each warp instruction adds 32 consecutive floats of a query row);
+    // the kernel is bound by shared-memory bandwidth, and this keeps the
+    // 2 x 32 KB per query tile of staging writes and bulk-copy reads out of it
+    // (backward 4.5 % faster on C3). D=64: an f32 staging tile in smem and a
+    // bulk tensor reduce-add (the per-row vector reds measured 20 % slower).
+    static constexpr bool DQ_RED = D == 128;
     static constexpr int DQS = BQ * D * 4;           // f32 dQ staging tile for the reduce-add
     // Two staging tiles: the L2 reduce-add of one tile (~0.75 us for 32 KB at
     // the chip's ~5.9 TB/s reduction rate, shared by all SMs) overlaps the
     // drain of the next.
-    static constexpr int NDQS = 2;
+    static constexpr int NDQS = DQ_RED ? 0 : 2;
     static constexpr int DQS_OFF = DS_OFF + NDS * DST;
     static constexpr int LSE_OFF = DQS_OFF + NDQS * DQS;
     static constexpr int DEL_OFF = LSE_OFF + QST * BQ * 4;
@@ -136,6 +147,7 @@ struct BwdParams {
     // respect to K before the rotary embedding (src/kernels/rope.rs:44-82).
     const float2* rope_tab;
     int hgroup;  // (batch, head) slices per dispatch group (see the block mapping)
+    float* dq_acc;  // [B*H][S][D] f32 accumulator (D=64: written through tdq by bulk reduce-adds)
     DeviceStatus* status;
 };
 
@@ -228,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&tk);
         prefetch_tmap(&tv);
         prefetch_tmap(&tdo);
-        prefetch_tmap(&tdq);
+        if (!C::DQ_RED) prefetch_tmap(&tdq);
     }
     tc_fence_before();
     __syncthreads();
@@ -581,16 +593,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncthreads();
     } else {
         // ------------------------------------------------------------ dQ drain warpgroup
-        // Each dQ tile goes TMEM -> registers -> f32 staging tile in smem, and one
-        // thread adds the tile into the accumulator with a bulk tensor reduce-add
-        // (the TMA unit does the read-modify-write in L2; no per-element atomics).
+        // Each dQ tile goes TMEM -> registers, then into the f32 accumulator in L2:
+        // D=128 by red.global.add from the registers; D=64 through an f32 staging
+        // tile in smem that one thread adds with a bulk tensor reduce-add (the TMA
+        // unit does the read-modify-write in L2).
         const int wi = warp % 4;
         const int r = wi * 32 + lane;  // TMEM lane: d (dQ^T) or query row (dQ)
         const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
         const bool elected = (warp == 12 && lane == 0);
         for (int it = 0; it < n_it; ++it) {
             const int buf = it % C::NDQ;
-            float* stage = (float*)(sm + C::DQS_OFF + (it % C::NDQS) * C::DQS);
             const int q0 = (i_start + it) * BQ;
             if (!mbar_wait(bar_addr(bars->dq_full[buf]), (it / C::NDQ) & 1, abort_flag, p.status, 70)) break;
             tc_fence_after();
@@ -600,19 +612,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             reg_fence<C::DQ_COLS>(v);
             tc_fence_before();
             mbar_arrive(bar_addr(bars->dq_empty[buf]));
-            // The reduce-add that used this staging tile (NDQS tiles ago) must
-            // have read it; the NDQS - 1 later ones may still be in flight.
-            if (elected) {
-                bulk_wait_group_read<C::NDQS - 1>();
-                mbar_arrive(bar_addr(bars->dqs_free));
-            }
-            if (!mbar_wait(bar_addr(bars->dqs_free), it & 1, abort_flag, p.status, 71)) break;
-            if (C::DQ_T) {
-                // staging [BQ queries][D] row-major: lane r = d, a warp writes 32 consecutive floats.
+            if constexpr (C::DQ_RED) {
+                static_assert(C::DQ_T, "the register drain adds dQ^T rows (lane = d)");
+                // a warp adds 32 consecutive floats of one query row per instruction
+                float* dst = p.dq_acc + ((int64_t)bh * p.S + q0) * D + r;
+                const int nq = min(BQ, p.S - q0);
 #pragma unroll
-                for (int c = 0; c < BQ; ++c) stage[c * D + r] = __uint_as_float(v[c]);
+                for (int c = 0; c < BQ; ++c)
+                    if (c < nq) red_add_f32(dst + (int64_t)c * D, __uint_as_float(v[c]));
             } else {
-                // staging = two 128B-swizzled boxes [BQ rows][32 floats]; lane r = query row.
+                static_assert(!C::DQ_T, "the staging drain writes dQ rows (lane = query row)");
+                float* stage = (float*)(sm + C::DQS_OFF + (it % C::NDQS) * C::DQS);
+                // The reduce-add that used this staging tile (NDQS tiles ago) must
+                // have read it; the NDQS - 1 later ones may still be in flight.
+                if (elected) {
+                    bulk_wait_group_read<C::NDQS - 1>();
+                    mbar_arrive(bar_addr(bars->dqs_free));
+                }
+                if (!mbar_wait(bar_addr(bars->dqs_free), it & 1, abort_flag, p.status, 71)) break;
+                // staging = D/32 128B-swizzled boxes [BQ rows][32 floats]; lane r = query row.
 #pragma unroll
                 for (int cb = 0; cb < D / 32; ++cb) {
                     uint8_t* row = (uint8_t*)stage + cb * (BQ * 128) + r * 128;
@@ -622,20 +640,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                             make_uint4(v[cb * 32 + 4 * j], v[cb * 32 + 4 * j + 1],
                                        v[cb * 32 + 4 * j + 2], v[cb * 32 + 4 * j + 3]);
                 }
-            }
-            fence_proxy_async();
-            mbar_arrive(bar_addr(bars->dqs_full));
-            if (elected) {
-                if (!mbar_wait(bar_addr(bars->dqs_full), it & 1, abort_flag, p.status, 72)) break;
-                if (C::DQ_T) {
-                    tma_reduce_add_3d(&tdq, smem_addr(stage), 0, q0, (int)bh);
-                } else {
+                fence_proxy_async();
+                mbar_arrive(bar_addr(bars->dqs_full));
+                if (elected) {
+                    if (!mbar_wait(bar_addr(bars->dqs_full), it & 1, abort_flag, p.status, 72)) break;
 #pragma unroll
                     for (int cb = 0; cb < D / 32; ++cb)
                         tma_reduce_add_3d(&tdq, smem_addr((uint8_t*)stage + cb * (BQ * 128)), cb * 32,
                                           q0, (int)bh);
+                    bulk_commit_group();
                 }
-                bulk_commit_group();
             }
         }
         if (elected) bulk_wait_group0();
@@ -775,12 +789,12 @@ cudaError_t launch(cudaStream_t st, int sm_count, DeviceStatus* status, const At
         !make_tmap_bhsd(&tk, k, d.B, d.H, d.S, D, d.sb, d.sh, d.ss, 64, BK) ||
         !make_tmap_bhsd(&tv, v, d.B, d.H, d.S, D, d.sb, d.sh, d.ss, 64, BK))
         return cudaErrorInvalidValue;
-    // dQ accumulator [B*H][S][D] f32: D=128 tiles are [BQ][128] plain, D=64 tiles are
+    // dQ accumulator [B*H][S][D] f32 for the bulk reduce-adds of the D=64 drain:
     // two [BQ][32] boxes with 128-byte swizzle (matches the staging writes).
-    const bool ok_dq = C::DQ_T
-        ? make_tmap_f32_3d(&tdq, w.dq_acc, D, d.S, (uint64_t)d.B * d.H, D, C::BQ, false)
-        : make_tmap_f32_3d(&tdq, w.dq_acc, D, d.S, (uint64_t)d.B * d.H, 32, C::BQ, true);
-    if (!ok_dq) return cudaErrorInvalidValue;
+    // The D=128 drain adds from registers and does not read the map.
+    memset(&tdq, 0, sizeof tdq);
+    if (!C::DQ_RED && !make_tmap_f32_3d(&tdq, w.dq_acc, D, d.S, (uint64_t)d.B * d.H, 32, C::BQ, true))
+        return cudaErrorInvalidValue;
     // setmaxnreg.inc waits until the warp's share fits the block's launch
     // allocation: launch only with exactly the register count the split assumes.
     {
@@ -810,6 +824,7 @@ cudaError_t launch(cudaStream_t st, int sm_count, DeviceStatus* status, const At
     prm.causal = causal;
     prm.rope_tab = rope_tab;
     prm.hgroup = HX_BWD_HGROUP;
+    prm.dq_acc = w.dq_acc;
     prm.status = status;
     const int64_t main_blocks = (int64_t)((d.S + BK - 1) / BK) * d.H * d.B;
     if (main_blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;  // past the grid's x limit

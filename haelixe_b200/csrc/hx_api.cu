@@ -680,6 +680,27 @@ static int gemm_rm(hx_ctx* c, cublasHandle_t h, hx_dtype dt, bool ta, bool tb, i
     return HX_OK;
 }
 
+// The bf16 GEMMs of the Linear layers run on this library's tcgen05 kernel
+// when its layout rules hold (16-byte aligned operands and rows); otherwise,
+// and for f32 (which the reference computes in f32 and this library keeps off
+// TF32), on cuBLAS. *done is set when the tcgen05 kernel took the product.
+static int gemm_tc(hx_ctx* c, hx_dtype dt, bool a_mn, bool b_mn, int m, int n, int k, const void* A, int lda,
+                   const void* B, int ldb, void* C, int ldc, const void* R, const void* bias, const char* who,
+                   bool* done) {
+    *done = false;
+    if (dt != HX_BF16 || c->gemm_backend != 0 ||
+        !hx::gemm_bf16_supported(a_mn, b_mn, m, n, k, A, lda, B, ldb, C, ldc, R, ldc, bias))
+        return HX_OK;
+    const int st = check_cuda(c, hx::gemm_bf16(c->stream, c->sm_count, c->status, a_mn, b_mn, m, n, k, A, lda, B,
+                                               ldb, C, ldc, R, ldc, bias),
+                              who);
+    if (st == HX_OK) {
+        *done = true;
+        c->last_gemm_path = 2;
+    }
+    return st;
+}
+
 static int linear_args(hx_ctx* c, hx_dtype dt, int rows, int in, int out, const char* who) {
     if (c == nullptr) return HX_ERR_INVALID;
     int st;
@@ -697,6 +718,11 @@ int hx_linear_fwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w, const vo
     DeviceGuard g(c->device);
     NvtxRange nv("hx_linear_fwd");
     LaunchCount lc(c);
+    bool done;
+    if ((st = gemm_tc(c, dt, false, true, rows, out_features, in_features, x, in_features, w, out_features, y,
+                      out_features, nullptr, b, "hx_linear_fwd", &done)) || done)
+        return st;
+    c->last_gemm_path = 1;
     cublasHandle_t h;
     if ((st = blas_for(c, &h))) return st;
     float beta = 0.f;
@@ -719,16 +745,32 @@ int hx_linear_bwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w, const vo
     DeviceGuard g(c->device);
     NvtxRange nv("hx_linear_bwd");
     LaunchCount lc(c);
-    cublasHandle_t h;
-    if ((st = blas_for(c, &h))) return st;
-    if (dx != nullptr &&  // dx[rows, in] = dy[rows, out] w[in, out]^T
-        (st = gemm_rm(c, h, dt, false, true, rows, in_features, out_features, dy, out_features, w, out_features,
-                      dx, in_features, 0.f, "hx_linear_bwd dx")))
-        return st;
-    if (dw != nullptr &&  // dw[in, out] = x[rows, in]^T dy[rows, out]
-        (st = gemm_rm(c, h, dt, true, false, in_features, out_features, rows, x, in_features, dy, out_features,
-                      dw, out_features, 0.f, "hx_linear_bwd dw")))
-        return st;
+    cublasHandle_t h = nullptr;
+    bool done = false;
+    if (dx != nullptr) {  // dx[rows, in] = dy[rows, out] w[in, out]^T
+        if ((st = gemm_tc(c, dt, false, false, rows, in_features, out_features, dy, out_features, w, out_features,
+                          dx, in_features, nullptr, nullptr, "hx_linear_bwd dx", &done)))
+            return st;
+        if (!done) {
+            c->last_gemm_path = 1;
+            if ((st = blas_for(c, &h)) ||
+                (st = gemm_rm(c, h, dt, false, true, rows, in_features, out_features, dy, out_features, w,
+                              out_features, dx, in_features, 0.f, "hx_linear_bwd dx")))
+                return st;
+        }
+    }
+    if (dw != nullptr) {  // dw[in, out] = x[rows, in]^T dy[rows, out]
+        if ((st = gemm_tc(c, dt, true, true, in_features, out_features, rows, x, in_features, dy, out_features,
+                          dw, out_features, nullptr, nullptr, "hx_linear_bwd dw", &done)))
+            return st;
+        if (!done) {
+            c->last_gemm_path = 1;
+            if ((!h && (st = blas_for(c, &h))) ||
+                (st = gemm_rm(c, h, dt, true, false, in_features, out_features, rows, x, in_features, dy,
+                              out_features, dw, out_features, 0.f, "hx_linear_bwd dw")))
+                return st;
+        }
+    }
     if (db != nullptr) {  // db[out] = sum over rows of dy
         void* scratch = nullptr;
         if ((st = hx_alloc(c, sizeof(float) * (uint64_t)hx::col_scratch_floats(rows, out_features), &scratch)))
@@ -820,6 +862,11 @@ int hx_linear_residual_fwd(hx_ctx* c, hx_dtype dt, const void* x, const void* w,
     DeviceGuard g(c->device);
     NvtxRange nv("hx_linear_residual_fwd");
     LaunchCount lc(c);
+    bool done;
+    if ((st = gemm_tc(c, dt, false, true, rows, out_features, in_features, x, in_features, w, out_features, y,
+                      out_features, residual, b, "hx_linear_residual_fwd", &done)) || done)
+        return st;
+    c->last_gemm_path = 1;
     cublasHandle_t h;
     if ((st = blas_for(c, &h))) return st;
     float beta = 0.f;
@@ -932,6 +979,14 @@ int hx_selftest_wait_timeout(hx_ctx* c) {
     NvtxRange nv("hx_selftest_wait_timeout");
     LaunchCount lc(c);
     return check_cuda(c, hx::selftest_wait_timeout(c->stream, c->status), "hx_selftest_wait_timeout");
+}
+
+int hx_last_gemm_path(const hx_ctx* c) { return c ? c->last_gemm_path : 0; }
+
+int hx_set_gemm_backend(hx_ctx* c, int backend) {
+    if (c == nullptr || (backend != 0 && backend != 1)) return HX_ERR_INVALID;
+    c->gemm_backend = backend;
+    return HX_OK;
 }
 
 int hx_set_force_simt(hx_ctx* c, int force) {

@@ -55,7 +55,9 @@ struct hx_ctx {
     std::mutex rope_mu;
     std::vector<hx::RopeTable> rope_tables;  // (cos, sin) tables, freed with the context
     std::mutex blas_mu;
-    void* blas = nullptr;  // cublasHandle_t for the Linear GEMMs, created on first use
+    void* blas = nullptr;  // cublasHandle_t for the f32 Linear GEMMs, created on first use
+    int gemm_backend = 0;  // bf16 Linear GEMMs: 0 = tcgen05 kernel where it applies, 1 = cuBLAS
+    int last_gemm_path = 0;  // 1 cuBLAS, 2 tcgen05 (the last Linear GEMM of this context)
 };
 
 namespace hx {
@@ -120,6 +122,16 @@ int64_t rmsnorm_bwd_scratch_floats(int64_t rows, int hidden);
 
 // ---- failure-path self-test (selftest.cu) ----
 cudaError_t selftest_wait_timeout(cudaStream_t st, DeviceStatus* status);
+
+// ---- tcgen05 GEMM (gemm_sm100.cu): row-major bf16, f32 accumulation ----
+// C[M,N] = A'[M,K] B'[K,N] (+ bias[N]) (+ R[M,N]); A' = A (K-major) or A^T
+// (a_mn), B' = B (b_mn, N contiguous) or B^T (K-major). cudaErrorNotSupported
+// when the operands do not meet TMA's layout rules (the caller uses cuBLAS).
+bool gemm_bf16_supported(bool a_mn, bool b_mn, int M, int N, int K, const void* A, int64_t lda, const void* B,
+                         int64_t ldb, const void* C, int64_t ldc, const void* R, int64_t ldr, const void* bias);
+cudaError_t gemm_bf16(cudaStream_t st, int sm_count, DeviceStatus* status, bool a_mn, bool b_mn, int M, int N,
+                      int K, const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                      const void* R, int64_t ldr, const void* bias);
 
 // ---- head reassembly (heads.cu) ----
 cudaError_t reassemble_heads(cudaStream_t st, int elem_bytes, const void* src, void* dst, int n,

@@ -116,6 +116,15 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
 // Plain bulk copy global -> this CTA's smem (16-byte aligned, size % 16 == 0).
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
                                           uint32_t bar) {
@@ -134,6 +143,11 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, uint32
         "r"(src), "r"(c0), "r"(c1), "r"(c2)
         : "memory");
 }
+// Fire-and-forget f32 add in L2 (no return value).
+__device__ __forceinline__ void red_add_f32(float* addr, float v) {
+    asm volatile("red.global.add.f32 [%0], %1;\n" ::"l"(addr), "f"(v) : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

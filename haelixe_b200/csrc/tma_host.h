@@ -80,4 +80,22 @@ inline bool make_tmap_2d(CUtensorMap* map, const void* base, int rows, int cols,
     return r == CUDA_SUCCESS;
 }
 
+// bf16 matrix [rows][cols] with a leading dimension of `ld` elements (ld >=
+// cols, ld * 2 a multiple of 16), box (box_cols, box_rows), 128B swizzle;
+// reads outside the matrix return 0.
+inline bool make_tmap_2d_ld(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                            int box_cols, int box_rows) {
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (fn == nullptr) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 }  // namespace hx

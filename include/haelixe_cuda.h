@@ -224,8 +224,11 @@ int hx_rope_bwd(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape, const v
 /* ---- the attention block around the kernel (src/nn/attention.rs:46-98) ------------ */
 /* y[rows, out] = x[rows, in] w[in, out] + b[out] (Linear::forward,
  * src/nn/linear.rs:54-56, weight stored [in, out] as in linear.rs:41); b may be
- * NULL. All row-major and contiguous. A cuBLAS GEMM with f32 accumulation and
- * no TF32 (the reference multiplies in f32, src/kernels/matmul.rs). */
+ * NULL. All row-major and contiguous, f32 accumulation. bf16: this library's
+ * tcgen05 GEMM (bias added in f32 before the one bf16 rounding) whenever the
+ * operands are 16-byte aligned with row lengths that are multiples of 8
+ * elements, else cuBLAS. f32: cuBLAS without TF32 (the reference multiplies
+ * in f32, src/kernels/matmul.rs). */
 int hx_linear_fwd(hx_ctx* ctx, hx_dtype dtype, const void* x, const void* w, const void* b, void* y,
                   int rows, int in_features, int out_features);
 /* Its backward: dx = dy w^T, dw = x^T dy, db = column sums of dy; each of
@@ -310,6 +313,59 @@ int hx_embedding_bwd(hx_ctx* ctx, hx_dtype dtype, const void* dout, const uint32
 int hx_reassemble_heads(hx_ctx* ctx, hx_dtype dtype, const void* shards, void* out, int n_shards,
                         int B, int H_shard, int S, int D, int out_layout);
 
+/* ---- the head-sharding exchange: NCCL all-gather + reassembly ------------------ */
+/* The reference runs on one device and has no collective. Its multi-head
+ * layer merges the per-head outputs after the attention
+ * (src/nn/attention.rs:91-94, transpose(1, 2) + view to [B, S, H*D]); with
+ * heads sharded across GPUs that merge needs every rank's heads, which these
+ * entry points gather over NCCL (NVLink / NVSwitch) and reassemble.
+ *
+ * A group holds NCCL communicator ranks: one per process
+ * (hx_group_create_rank, the id from hx_group_unique_id shared by the
+ * caller) or all of them in one process (hx_group_create; drive each member
+ * from its own host thread). NCCL is loaded at run time (libnccl.so.2);
+ * without it these return HX_ERR_UNSUPPORTED. Every call that can wait on a
+ * peer (initialisation, a gather, hx_group_sync) gives up after timeout_ms:
+ * the communicator is aborted and HX_ERR_NCCL returned, with the reason in
+ * hx_group_last_error; an aborted group only accepts hx_group_destroy.
+ * flags: HX_GROUP_REGISTER registers the gather buffer with NCCL
+ * (ncclCommRegister); HX_GROUP_SYMMETRIC registers it as a symmetric window
+ * (collective, NCCL >= 2.27); HX_GROUP_COPY_ENGINE asks NCCL >= 2.28 to run
+ * collectives on the copy engines where it can (CTA policy "zero"). */
+#define HX_GROUP_ID_BYTES 128
+typedef struct hx_group hx_group;
+enum { HX_GROUP_REGISTER = 1, HX_GROUP_SYMMETRIC = 2, HX_GROUP_COPY_ENGINE = 4 };
+/* Writes HX_GROUP_ID_BYTES bytes (an ncclUniqueId) to id. */
+int hx_group_unique_id(void* id);
+/* This process's rank `rank` of `nranks`, on `device`. *out is set even on
+ * failure (for hx_group_last_error); destroy it either way. */
+int hx_group_create_rank(int device, int nranks, int rank, const void* id, int flags, int timeout_ms,
+                         hx_group** out);
+/* All n ranks in this process, rank i on devices[i] (distinct devices). */
+int hx_group_create(int n, const int* devices, int flags, int timeout_ms, hx_group** out);
+int hx_group_destroy(hx_group* group);
+int hx_group_abort(hx_group* group);
+int hx_group_set_timeout(hx_group* group, int timeout_ms);
+int hx_group_info(const hx_group* group, int* nranks, int* members, int* nccl_version);
+int hx_group_last_error(const hx_group* group, char* buf, uint64_t n);
+/* Device buffer of nranks packed slots of slot_bytes each (rank r's slot at
+ * base + r * slot_bytes), owned by the group. A shard written into the
+ * member's own slot is gathered in place. Collective when the group was made
+ * with HX_GROUP_SYMMETRIC. */
+int hx_group_gather_buffer(hx_group* group, int member, uint64_t slot_bytes, void** base);
+/* Gathers every rank's shard [B, H_shard, S, D] (contiguous) into the gather
+ * buffer and, if merged is not NULL, reassembles it as [B, H, S, D]
+ * (layout 0) or [B, S, H, D] (layout 1), H = nranks * H_shard. Runs on the
+ * member's own side stream, after the work already queued on ctx's stream;
+ * it returns once the work is enqueued. Order later work on ctx's stream
+ * after it with hx_group_wait, or block the host with hx_group_sync. */
+int hx_allgather_heads(hx_group* group, int member, hx_ctx* ctx, hx_dtype dtype, const void* shard,
+                       void* merged, int B, int H_shard, int S, int D, int layout);
+/* Makes ctx's stream wait (on the device) for the member's last gather. */
+int hx_group_wait(hx_group* group, int member, hx_ctx* ctx);
+/* Blocks the host until the member's last gather is done, or the timeout. */
+int hx_group_sync(hx_group* group, int member);
+
 /* ---- diagnostics --------------------------------------------------------------- */
 /* Number of kernels this context has launched so far. */
 uint64_t hx_kernel_launches(const hx_ctx* ctx);
@@ -318,6 +374,12 @@ uint64_t hx_kernel_launches(const hx_ctx* ctx);
 int hx_last_path(const hx_ctx* ctx);
 /* Forces the SIMT kernels (1) or restores automatic selection (0). */
 int hx_set_force_simt(hx_ctx* ctx, int force);
+/* Which GEMM ran the last Linear product on this context: 0 none, 1 cuBLAS,
+ * 2 the tcgen05 kernel. */
+int hx_last_gemm_path(const hx_ctx* ctx);
+/* bf16 Linear GEMMs: 0 = the tcgen05 kernel where it applies (default),
+ * 1 = always cuBLAS. */
+int hx_set_gemm_backend(hx_ctx* ctx, int backend);
 /* Exercises the kernels' failure path: enqueues one CTA whose bounded
  * mbarrier wait can never complete. After the wait limit (2 s) it records the
  * expiry in the context's status word and exits normally (no trap, no hang),

@@ -25,6 +25,7 @@ typedef struct {
     const REAL* b;
     REAL* out;
     long m, k, n;
+    int accumulate; /* 1: add onto `out` instead of starting from zero */
 } FN(mm_ctx);
 
 static void FN(mm_task)(void* vctx, long bm0, long bm1) {
@@ -33,9 +34,11 @@ static void FN(mm_task)(void* vctx, long bm0, long bm1) {
     for (long bm = bm0; bm < bm1; ++bm) {
         const long m_start = bm * ORA_BLOCK;
         const long m_end = (m_start + ORA_BLOCK) < m ? (m_start + ORA_BLOCK) : m;
-        for (long i = m_start; i < m_end; ++i) {
-            REAL* row = c->out + i * n;
-            for (long j = 0; j < n; ++j) row[j] = (REAL)0;
+        if (!c->accumulate) {
+            for (long i = m_start; i < m_end; ++i) {
+                REAL* row = c->out + i * n;
+                for (long j = 0; j < n; ++j) row[j] = (REAL)0;
+            }
         }
         for (long n_start = 0; n_start < n; n_start += ORA_BLOCK) {
             const long n_end = (n_start + ORA_BLOCK) < n ? (n_start + ORA_BLOCK) : n;
@@ -58,7 +61,14 @@ static void FN(mm_task)(void* vctx, long bm0, long bm1) {
 }
 
 static void FN(matmul)(const REAL* a, const REAL* b, REAL* out, long m, long k, long n) {
-    FN(mm_ctx) c = {a, b, out, m, k, n};
+    FN(mm_ctx) c = {a, b, out, m, k, n, 0};
+    ora_parallel_for((m + ORA_BLOCK - 1) / ORA_BLOCK, FN(mm_task), &c);
+}
+
+/* out += a . b, with each output element's terms added in the same k order
+ * as `matmul` (used to sum a product over consecutive row blocks of k). */
+static void FN(matmul_acc)(const REAL* a, const REAL* b, REAL* out, long m, long k, long n) {
+    FN(mm_ctx) c = {a, b, out, m, k, n, 1};
     ora_parallel_for((m + ORA_BLOCK - 1) / ORA_BLOCK, FN(mm_task), &c);
 }
 
@@ -254,6 +264,91 @@ int FN(ora_attn_bwd)(const float* q, const float* k, const float* v, const float
         FN(to_float)(outs, dk + off, s * d);
     }
     free(qs); free(ks); free(vs); free(dos); free(outs); free(p); free(a); free(b);
+    return 0;
+}
+
+/* Forward and backward together, over blocks of `rows` query rows, for
+ * sequences whose S x S matrices do not fit in host memory (S = 32768 needs
+ * 4 GiB per matrix). The formulas and the order of every sum are those of
+ * ora_attn_fwd and ora_attn_bwd above (src/ops/flash_attention.rs:16-39),
+ * so the results are the same bit for bit:
+ *   * softmax and its backward are row-wise, so a block of rows sees exactly
+ *     the rows of the full matrix;
+ *   * under the causal mask the keys past the block's last row have P = 0
+ *     and dS = 0 for every row of the block; they only add zeros to the
+ *     full-matrix sums, so they are left out (keys [0, i1) for rows [i0, i1));
+ *   * dK = dS^T Q and dV = P^T dO sum over query rows; the blocks are
+ *     visited in order and each adds its rows in order (matmul_acc), which is
+ *     the order of the full-matrix product; the scale is applied once at the
+ *     end, as in ora_attn_bwd.
+ * o, lse (may be NULL), dq, dk, dv: outputs, [BH, S, D] and [BH, S]. */
+int FN(ora_attn_rows)(const float* q, const float* k, const float* v, const float* dout, float* o,
+                      float* lse, float* dq, float* dk, float* dv, int BH, int S, int D, float scale,
+                      int causal, int rows) {
+    const long s = S, d = D;
+    const long R = rows > 0 ? (rows < S ? rows : S) : S;
+    REAL* qs = (REAL*)malloc(sizeof(REAL) * s * d);
+    REAL* ks = (REAL*)malloc(sizeof(REAL) * s * d);
+    REAL* vs = (REAL*)malloc(sizeof(REAL) * s * d);
+    REAL* dos = (REAL*)malloc(sizeof(REAL) * s * d);
+    REAL* dks = (REAL*)malloc(sizeof(REAL) * s * d);
+    REAL* dvs = (REAL*)malloc(sizeof(REAL) * s * d);
+    REAL* outs = (REAL*)malloc(sizeof(REAL) * R * d);
+    REAL* tr = (REAL*)malloc(sizeof(REAL) * s * d);   /* K^T or V^T of the block's keys */
+    REAL* p = (REAL*)malloc(sizeof(REAL) * R * s);    /* P of the block */
+    REAL* dp = (REAL*)malloc(sizeof(REAL) * R * s);   /* dP, then dS */
+    REAL* pt = (REAL*)malloc(sizeof(REAL) * R * s);   /* a transposed block */
+    if (!qs || !ks || !vs || !dos || !dks || !dvs || !outs || !tr || !p || !dp || !pt) {
+        free(qs); free(ks); free(vs); free(dos); free(dks); free(dvs); free(outs); free(tr);
+        free(p); free(dp); free(pt);
+        return -1;
+    }
+    for (long bh = 0; bh < BH; ++bh) {
+        const long off = bh * s * d;
+        FN(to_real)(q + off, qs, s * d);
+        FN(to_real)(k + off, ks, s * d);
+        FN(to_real)(v + off, vs, s * d);
+        FN(to_real)(dout + off, dos, s * d);
+        for (long i = 0; i < s * d; ++i) dks[i] = dvs[i] = (REAL)0;
+        for (long i0 = 0; i0 < s; i0 += R) {
+            const long i1 = (i0 + R) < s ? (i0 + R) : s;
+            const long rb = i1 - i0;
+            const long sk = causal ? i1 : s; /* keys that can be unmasked in this block */
+            const REAL* qb = qs + i0 * d;
+            const REAL* dob = dos + i0 * d;
+            /* P = softmax(scale Q K^T [mask]) for rows [i0, i1) */
+            FN(transpose)(ks, tr, sk, d);
+            FN(matmul)(qb, tr, p, rb, d, sk);
+            FN(scale_inplace)(p, rb * sk, (REAL)scale);
+            if (causal) {
+                for (long r = 0; r < rb; ++r)
+                    for (long j = i0 + r + 1; j < sk; ++j) p[r * sk + j] = -(REAL)INFINITY;
+            }
+            FN(softmax_rows_inplace)(p, lse ? lse + bh * s + i0 : NULL, rb, sk);
+            /* O = P V */
+            FN(matmul)(p, vs, outs, rb, sk, d);
+            FN(to_float)(outs, o + off + i0 * d, rb * d);
+            /* dV += P^T dO */
+            FN(transpose)(p, pt, rb, sk);
+            FN(matmul_acc)(pt, dob, dvs, sk, rb, d);
+            /* dP = dO V^T, then dS = softmax_backward(dP, P) */
+            FN(transpose)(vs, tr, sk, d);
+            FN(matmul)(dob, tr, dp, rb, d, sk);
+            FN(softmax_backward_inplace)(dp, p, rb, sk);
+            /* dQ = dS K * scale */
+            FN(matmul)(dp, ks, outs, rb, sk, d);
+            FN(scale_inplace)(outs, rb * d, (REAL)scale);
+            FN(to_float)(outs, dq + off + i0 * d, rb * d);
+            /* dK += dS^T Q */
+            FN(transpose)(dp, pt, rb, sk);
+            FN(matmul_acc)(pt, qb, dks, sk, rb, d);
+        }
+        FN(scale_inplace)(dks, s * d, (REAL)scale);
+        FN(to_float)(dks, dk + off, s * d);
+        FN(to_float)(dvs, dv + off, s * d);
+    }
+    free(qs); free(ks); free(vs); free(dos); free(dks); free(dvs); free(outs); free(tr);
+    free(p); free(dp); free(pt);
     return 0;
 }
 

@@ -39,6 +39,9 @@ def lib():
         L.ora_attn_bwd.argtypes = [_F, _F, _F, _F, _F, _F, _F, i, i, i, f, i, i]
         L.ora_attn_bwd_f64.argtypes = L.ora_attn_bwd.argtypes
         L.ora_attn_fwd.restype = L.ora_attn_fwd_f64.restype = i
+        L.ora_attn_rows.argtypes = [_F, _F, _F, _F, _F, _F, _F, _F, _F, i, i, i, f, i, i]
+        L.ora_attn_rows_f64.argtypes = L.ora_attn_rows.argtypes
+        L.ora_attn_rows.restype = L.ora_attn_rows_f64.restype = i
         L.ora_attn_bwd.restype = L.ora_attn_bwd_f64.restype = i
         L.ora_softmax.argtypes = [_F, _F, l, l]
         L.ora_softmax_backward.argtypes = [_F, _F, _F, l, l]
@@ -117,6 +120,22 @@ def attn_bwd(q, k, v, do, scale: float, causal: bool, f64: bool = False, ref_com
     if rc != 0:
         raise MemoryError("oracle backward could not allocate its S x S buffers")
     return dq, dk, dv
+
+
+def attn_rows(q, k, v, do, scale: float, causal: bool, rows: int = 2048, f64: bool = False):
+    """(O, LSE, dQ, dK, dV) by blocks of `rows` query rows: the results of
+    attn_fwd and attn_bwd bit for bit, without S x S buffers, so that a whole
+    S = 32768 slice fits in host memory (3 x rows x S floats of scratch)."""
+    q, k, v, do = _f32(q), _f32(k), _f32(v), _f32(do)
+    BH, S, D = q.shape
+    o, dq, dk, dv = (np.empty_like(q) for _ in range(4))
+    lse = np.empty((BH, S), np.float32)
+    fn = lib().ora_attn_rows_f64 if f64 else lib().ora_attn_rows
+    rc = fn(_p(q), _p(k), _p(v), _p(do), _p(o), _p(lse), _p(dq), _p(dk), _p(dv), BH, S, D,
+            float(scale), int(bool(causal)), int(rows))
+    if rc != 0:
+        raise MemoryError("oracle could not allocate its row-block buffers")
+    return o, lse, dq, dk, dv
 
 
 def rope_fwd(x, base: float) -> np.ndarray:

@@ -265,58 +265,77 @@ def test_autograd_node_with_rope():
     _check("dV", vd.grad, rdv, torch.bfloat16)
 
 
-def _sampled_full_size(B, H, S, D, causal, rope_base=None, samples=((0, 0),), prefix=None):
-    """Full-size run on the GPU; oracle on sampled (b, h) slices; identities on all.
-    With `prefix` (causal only) the sampled slices are checked on their first
-    `prefix` rows instead: under the causal mask, O and dQ of query rows
-    < prefix depend only on keys < prefix, so the oracle runs on the prefix."""
+def _sampled_full_size(B, H, S, D, causal, rope_base=None, samples=((0, 0),)):
+    """Full-size run on the GPU; the oracle on whole sampled (b, h) slices
+    (every query row, O, dQ, dK and dV), and gradient identities on every head.
+
+    The oracle is the row-block restatement (oracle.attn_rows: the plain
+    oracle's results bit for bit, without S x S buffers). With `rope_base`
+    the GPU rotates Q and K (hx.rope_forward) and folds the inverse rotation
+    into dQ and dK (attn_backward(..., rope_base)), as the benchmark step does;
+    the oracle rotates the same unrotated inputs with its own RoPE
+    (src/kernels/rope.rs:5-44), rounds them to bf16 as the GPU stores them,
+    and rotates its dQ, dK back (rope.rs:46-82). Returns the max-abs error
+    of each checked tensor."""
     torch.manual_seed(0)
     g = torch.Generator(device="cuda").manual_seed(1234)
-    q, k, v, do = (torch.randn(B, H, S, D, device="cuda", generator=g).to(torch.bfloat16)
-                   for _ in range(4))
+    q0, k0, v, do = (torch.randn(B, H, S, D, device="cuda", generator=g).to(torch.bfloat16)
+                     for _ in range(4))
+    q, k = q0, k0
     if rope_base is not None:
-        q = hx.rope_forward(q, rope_base)
-        k = hx.rope_forward(k, rope_base)
+        q = hx.rope_forward(q0, rope_base)
+        k = hx.rope_forward(k0, rope_base)
     scale = 1.0 / math.sqrt(D)
     o, lse = hx.attn_forward(q, k, v, scale, causal)
-    dq, dk, dv = hx.attn_backward(q, k, v, o, lse, do, scale, causal)
+    dq, dk, dv = hx.attn_backward(q, k, v, o, lse, do, scale, causal, rope_base=rope_base)
     torch.cuda.synchronize()
-    # identities over every head: sum_j dK_j = 0, sum_j dV_j = sum_i dO_i
-    dks, dk_l1 = dk.float().sum(2), dk.float().abs().sum(2)
-    assert (dks.abs() <= 0.02 * dk_l1 + 1e-3).all(), (dks.abs() / dk_l1).max().item()
+    # identities over every head: sum_j dK_j = 0 (for K as the attention sees
+    # it, so not after the inverse rotation), sum_j dV_j = sum_i dO_i
+    if rope_base is None:
+        dks, dk_l1 = dk.float().sum(2), dk.float().abs().sum(2)
+        assert (dks.abs() <= 0.02 * dk_l1 + 1e-3).all(), (dks.abs() / dk_l1).max().item()
     dvs, dos = dv.float().sum(2), do.float().sum(2)
     dv_l1 = dv.float().abs().sum(2)
     assert ((dvs - dos).abs() <= 0.02 * dv_l1 + 1e-2).all(), ((dvs - dos).abs() / dv_l1).max().item()
+    errs = {}
     for (b, h) in samples:
-        if prefix is not None:
-            assert causal
-            sl = [t[b, h, :prefix].float().cpu().numpy()[None] for t in (q, k, v, do)]
-            ro, _ = ora.attn_fwd(*sl[:3], scale, causal)
-            rdq = ora.attn_bwd(*sl, scale, causal)[0]
-            _check(f"O[{b},{h},:{prefix}]", o[b, h, :prefix], ro[0], torch.bfloat16)
-            _check(f"dQ[{b},{h},:{prefix}]", dq[b, h, :prefix], rdq[0], torch.bfloat16)
-            continue
-        sl = [t[b, h].float().cpu().numpy()[None] for t in (q, k, v, do)]
-        ro, _ = ora.attn_fwd(*sl[:3], scale, causal)
-        rg = ora.attn_bwd(*sl, scale, causal)
-        _check(f"O[{b},{h}]", o[b, h], ro[0], torch.bfloat16)
-        for name, got, ref in zip(("dQ", "dK", "dV"), (dq, dk, dv), rg):
-            _check(f"{name}[{b},{h}]", got[b, h], ref[0], torch.bfloat16)
+        sl = [t[b, h].float().cpu().numpy()[None] for t in (q0, k0, v, do)]
+        if rope_base is not None:
+            qr, kr = ora.rope_fwd(sl[0], rope_base), ora.rope_fwd(sl[1], rope_base)
+            errs[f"RoPE(Q)[{b},{h}]"] = _check(f"RoPE(Q)[{b},{h}]", q[b, h], qr[0], torch.bfloat16)
+            errs[f"RoPE(K)[{b},{h}]"] = _check(f"RoPE(K)[{b},{h}]", k[b, h], kr[0], torch.bfloat16)
+            sl[0], sl[1] = ora.round_bf16(qr), ora.round_bf16(kr)
+        ro, rlse, rdq, rdk, rdv = ora.attn_rows(*sl, scale, causal)
+        if rope_base is not None:
+            rdq, rdk = ora.rope_bwd(rdq, rope_base), ora.rope_bwd(rdk, rope_base)
+        errs[f"O[{b},{h}]"] = _check(f"O[{b},{h}]", o[b, h], ro[0], torch.bfloat16)
+        lse_bh = lse.view(B, H, S)[b, h].cpu().numpy()
+        errs[f"LSE[{b},{h}]"] = float(np.max(np.abs(lse_bh - rlse[0])))
+        assert errs[f"LSE[{b},{h}]"] < 1e-3
+        for name, got, ref in zip(("dQ", "dK", "dV"), (dq, dk, dv), (rdq, rdk, rdv)):
+            errs[f"{name}[{b},{h}]"] = _check(f"{name}[{b},{h}]", got[b, h], ref[0], torch.bfloat16)
+    print(f"max-abs errors B{B} H{H} S{S} D{D} {'causal' if causal else 'full'}"
+          f"{'' if rope_base is None else f' rope {rope_base:g}'}: "
+          + ", ".join(f"{k}={v:.3g}" for k, v in errs.items()))
+    return errs
 
 
 def test_standalone_op_b8_h16_s2048_d64_causal():
-    _sampled_full_size(8, 16, 2048, 64, True, samples=((0, 0), (7, 15)))
+    _sampled_full_size(8, 16, 2048, 64, True, samples=((0, 0), (3, 9), (7, 15)))
 
 
 def test_llama_layer_b4_h32_s8192_d128_causal_rope():
-    _sampled_full_size(4, 32, 8192, 128, True, rope_base=500000.0, samples=((3, 31),))
+    """The benchmark step's configuration: RoPE theta 500000 on the GPU against
+    the oracle's RoPE at every position of the slice (angles up to 8191 rad),
+    then attention, then the fused inverse rotation, on three whole slices."""
+    _sampled_full_size(4, 32, 8192, 128, True, rope_base=500000.0, samples=((0, 0), (1, 17), (3, 31)))
 
 
 def test_long_context_b1_h64_s32768_d128_causal():
     """The long-context configuration at full size (64 heads x 32768): the
-    gradient identities on every head, and O and dQ of the first 2048 query
-    rows of two heads against the oracle (causal prefix consistency)."""
-    _sampled_full_size(1, 64, 32768, 128, True, samples=((0, 0), (0, 63)), prefix=2048)
+    gradient identities on every head, and O, dQ, dK, dV of two whole heads
+    (all 32768 query rows) against the oracle."""
+    _sampled_full_size(1, 64, 32768, 128, True, samples=((0, 0), (0, 63)))
 
 
 def test_full_mask_long_sequences():

@@ -7,6 +7,8 @@
 3. Attention gradients against finite differences (EPS/TOL of the reference).
 4. An independent implementation (torch CPU, f64 autograd) of the same math.
 5. The documented departures from the reference (scale on dQ/dK, causal mask).
+6. The row-block restatement (used for slices too long for S x S buffers)
+   against the plain oracle, bit for bit.
 """
 import json
 import math
@@ -87,6 +89,20 @@ def test_f32_port_matches_f64(S, D, causal):
     g64 = ora.attn_bwd(q, k, v, do, scale, causal, f64=True)
     for a, b in zip(g32, g64):
         assert np.max(np.abs(a - b)) < 5e-5
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("BH,S,D,rows", [(2, 1, 64, 64), (2, 300, 64, 128), (1, 1000, 128, 256),
+                                         (1, 1000, 128, 192), (2, 513, 64, 64), (1, 4096, 128, 1024),
+                                         (1, 129, 32, 4096)])
+def test_row_block_oracle_is_the_plain_oracle_bit_for_bit(BH, S, D, rows, causal):
+    q, k, v, do = _inputs(BH, S, D, seed=3 * S + D)
+    scale = 1.0 / math.sqrt(D)
+    o, lse = ora.attn_fwd(q, k, v, scale, causal)
+    g = ora.attn_bwd(q, k, v, do, scale, causal)
+    got = ora.attn_rows(q, k, v, do, scale, causal, rows)
+    for name, a, b in zip(("O", "LSE", "dQ", "dK", "dV"), (o, lse) + g, got):
+        assert np.array_equal(a, b), (name, float(np.abs(a - b).max()))
 
 
 @pytest.mark.parametrize("causal", [False, True])
