@@ -90,6 +90,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--workload", choices=["attention", "block_stack"], default="attention")
+    p.add_argument("--rope-launches", type=int, choices=[1, 2], default=2,
+                   help="rotate Q and K in two launches (hx_rope_fwd) or in one (hx_rope_fwd_qk)")
     p.add_argument("--exchange-flags", type=int, default=0,
                    help="hx_group flags of the N>1 exchange: 1 register, 2 symmetric window, 4 copy engines")
     return p.parse_args()
@@ -357,8 +359,11 @@ def run_haelixe(a):
             ev.setdefault("f0", []).append(torch.cuda.Event(enable_timing=True))
             ev.setdefault("f1", []).append(torch.cuda.Event(enable_timing=True))
             ev.setdefault("b1", []).append(torch.cuda.Event(enable_timing=True))
-        hx.rope_forward(q, a.rope_theta, out=qr)
-        hx.rope_forward(k, a.rope_theta, out=kr)
+        if a.rope_launches == 1:
+            hx.rope_forward_qk(q, k, a.rope_theta, out_q=qr, out_k=kr)
+        else:
+            hx.rope_forward(q, a.rope_theta, out=qr)
+            hx.rope_forward(k, a.rope_theta, out=kr)
         if timed:
             ev["f0"][-1].record(stream)
         hx.attn_forward(qr, kr, v, scale, causal, out=o, lse=lse)

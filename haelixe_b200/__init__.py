@@ -20,6 +20,7 @@ from .attention import (  # noqa: F401
     flash_attention,
     rope_backward,
     rope_forward,
+    rope_forward_qk,
 )
 from ._native import HxError  # noqa: F401
 from . import nn, optim  # noqa: F401

@@ -110,6 +110,7 @@ SIGNATURES = {
     "hx_gelu_bwd": (_I, [_P, _I, _P, _P, _P, _U64]),
     "hx_rope_fwd": (_I, [_P, _I, _SHP, _P, _P, _F]),
     "hx_rope_bwd": (_I, [_P, _I, _SHP, _P, _P, _F]),
+    "hx_rope_fwd_qk": (_I, [_P, _I, _SHP, _P, _P, _P, _P, _F]),
     "hx_reassemble_heads": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _I, _I]),
     "hx_group_unique_id": (_I, [_P]),
     "hx_group_create_rank": (_I, [_I, _I, _I, _P, _I, _I, ctypes.POINTER(_P)]),

@@ -290,6 +290,26 @@ def rope_forward(x: torch.Tensor, base: float, out: Optional[torch.Tensor] = Non
     return out
 
 
+def rope_forward_qk(q: torch.Tensor, k: torch.Tensor, base: float, out_q: Optional[torch.Tensor] = None,
+                    out_k: Optional[torch.Tensor] = None):
+    """rope_forward of q and k (same shape and strides) in one launch."""
+    _check_operands(q, k)
+    if q.shape != k.shape or q.stride() != k.stride():
+        raise ValueError("q and k must have the same shape and strides")
+    ctx = context(q.device.index)
+    ctx.use_stream()
+    _check_outputs(q, out_q)
+    _check_outputs(k, out_k)
+    out_q = _like(q) if out_q is None else out_q
+    out_k = _like(k) if out_k is None else out_k
+    if out_q.stride() != q.stride() or out_k.stride() != k.stride():
+        raise ValueError("outputs must have the strides of the inputs")
+    shp = _shape_of(q)
+    N.check(N.lib().hx_rope_fwd_qk(ctx.handle, _DTYPES[q.dtype], ctypes.byref(shp), _ptr(q), _ptr(k),
+                                   _ptr(out_q), _ptr(out_k), float(base)), ctx.handle)
+    return out_q, out_k
+
+
 def rope_backward(g: torch.Tensor, base: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Inverse rotation (kernels/rope.rs:46-82)."""
     _check_operands(g)

@@ -11,16 +11,22 @@
 // dW = x^T dy; UMMA reads both majors straight from the TMA tiles, so no
 // operand is transposed in memory.
 //
-// Persistent kernel, one CTA per SM, 256 threads:
-//   warp 0     TMA producer: per 64-wide K block, the A tile (128 x 64) and
+// Persistent kernel, one CTA per SM, tiles of BM x BN (BM = 128 or 256):
+//   warp 0     TMA producer: per 64-wide K block, the A tile (BM x 64) and
 //              the B tile (BN x 64), 128-byte swizzle, into a STAGES ring;
-//   warp 1     MMA issuer (one thread): 4 UMMAs (M=128, N=BN, K=16) per K
-//              block into one of two TMEM accumulators (2 x BN columns), so
+//   warp 1     MMA issuer (one thread): per K block and 128-row half of A,
+//              4 UMMAs (M=128, N=BN, K=16); the B tile in smem serves both
+//              halves, so a 256 x 256 tile reads a third less operand data
+//              from L2 per FLOP than a 128 x 256 one (the kernel is bound by
+//              L2 -> SM bandwidth when K is small). With BM = 128 the two
+//              TMEM accumulators (2 x BN columns) alternate between tiles so
 //              the epilogue of tile t overlaps the main loop of tile t + 1;
+//              with BM = 256 the two halves fill TMEM and the epilogue is
+//              exposed once per tile;
 //   warp 2     TMEM allocation;
-//   warps 4-7  epilogue: thread = output row (TMEM lane), 32 columns per
-//              tcgen05.ld, + bias + residual in f32, one bf16 rounding,
-//              16-byte stores.
+//   warps 4-7 (and 8-11 for BM = 256)  epilogue: thread = output row (TMEM
+//              lane), 32 columns per tcgen05.ld, + bias + residual in f32,
+//              one bf16 rounding, 16-byte stores.
 // Tiles are visited in groups of 8 M-tiles (consecutive CTAs share B tiles
 // in L2). All mbarrier waits are bounded (sm100_ptx.cuh).
 #include "sm100_ptx.cuh"
@@ -31,19 +37,23 @@ namespace {
 
 using namespace ptx;
 
-constexpr int GBM = 128;  // UMMA M, rows per tile
 constexpr int GBK = 64;   // K per stage (one 128-byte swizzle atom of bf16)
-constexpr int kGemmThreads = 256;
 constexpr int kGroupM = 8;
 
-template <int BN>
+template <int BM, int BN>
 struct GCfg {
-    static constexpr int A_BYTES = GBM * GBK * 2;
+    static constexpr int HALVES = BM / 128;            // UMMA M = 128 per half
+    static constexpr int NBUF = HALVES == 1 ? 2 : 1;   // accumulator sets (alternating tiles)
+    static constexpr int TMEM_COLS = NBUF * HALVES * BN;
+    static constexpr int THREADS = 128 + HALVES * 128;
+    static constexpr int A_HALF = 128 * GBK * 2;
+    static constexpr int A_BYTES = HALVES * A_HALF;
     static constexpr int B_BYTES = BN * GBK * 2;
     static constexpr int STAGE = A_BYTES + B_BYTES;
-    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int STAGES = 196608 / STAGE < 8 ? 196608 / STAGE : 8;
     static constexpr int BAR_OFF = STAGES * STAGE;
     static constexpr int SMEM = BAR_OFF + 256 + 1024;
+    static_assert(TMEM_COLS <= 512, "tensor memory");
     static_assert(SMEM <= 232448, "shared memory per block");
     static_assert(STAGE % 1024 == 0, "stage buffers on 1024-byte boundaries");
 };
@@ -79,11 +89,11 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
     nt = in / gm;
 }
 
-template <int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+template <int BM, int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(GCfg<BM, BN>::THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                      const GemmParams p) {
-    using C = GCfg<BN>;
+    using C = GCfg<BM, BN>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* sm = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     GBars* bars = (GBars*)(sm + C::BAR_OFF);
@@ -100,14 +110,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(gbar(bars->acc_full[b]), 1);
-            mbar_init(gbar(bars->acc_empty[b]), 128);
+            mbar_init(gbar(bars->acc_empty[b]), C::HALVES * 128);
         }
         mbar_init(gbar(bars->done), 1);
         fence_mbar_init();
         fence_proxy_async();
     }
     if (warp == 2) {
-        tmem_alloc(smem_addr(&bars->tmem_base), 2 * BN);
+        tmem_alloc(smem_addr(&bars->tmem_base), C::TMEM_COLS);
         tmem_relinquish();
     }
     if (warp == 0 && lane == 0) {
@@ -127,7 +137,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
                 int mt, nt;
                 tile_coords(t, p.tiles_m, p.tiles_n, mt, nt);
-                const int m0 = mt * GBM, n0 = nt * BN;
+                const int m0 = mt * BM, n0 = nt * BN;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     if (!(ok = mbar_wait(gbar(bars->empty[s]), ((it / C::STAGES) & 1) ^ 1, abort_flag,
@@ -137,11 +147,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     mbar_arrive_expect_tx(fb, C::STAGE);
                     const uint32_t sa = smem_addr(sm + s * C::STAGE), sb = sa + C::A_BYTES;
                     const int k0 = kb * GBK;
-                    if (A_MN) {  // two boxes of 64 M x 64 K
-                        tma_load_2d(sa, &ta, fb, m0, k0);
-                        tma_load_2d(sa + 8192, &ta, fb, m0 + 64, k0);
-                    } else {     // one box of 64 K x 128 M
-                        tma_load_2d(sa, &ta, fb, k0, m0);
+                    if (A_MN) {  // BM/64 boxes of 64 M x 64 K (a half = two boxes)
+#pragma unroll
+                        for (int c = 0; c < BM / 64; ++c) tma_load_2d(sa + c * 8192, &ta, fb, m0 + c * 64, k0);
+                    } else {     // one box of 64 K x 128 M per half
+#pragma unroll
+                        for (int h = 0; h < C::HALVES; ++h) tma_load_2d(sa + h * C::A_HALF, &ta, fb, k0, m0 + h * 128);
                     }
                     if (B_MN) {  // BN/64 boxes of 64 N x 64 K
 #pragma unroll
@@ -159,7 +170,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16_f32(GBM, BN, A_MN, B_MN);
+            constexpr uint32_t idesc = idesc_bf16_f32(128, BN, A_MN, B_MN);
             const uint32_t s0 = smem_addr(sm);
             // A: K-major 128 rows x 128 B (SBO 1024, K step 32 B) or MN-major
             // two 64-element chunks 8 KB apart (LBO 8192, SBO 1024, K step 2 KB).
@@ -171,11 +182,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int it = 0, lt = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++lt) {
-                const int b = lt & 1;
-                if (!(ok = mbar_wait(gbar(bars->acc_empty[b]), ((lt >> 1) & 1) ^ 1, abort_flag, p.status, 81)))
+                const int b = lt % C::NBUF;
+                if (!(ok = mbar_wait(gbar(bars->acc_empty[b]), ((lt / C::NBUF) & 1) ^ 1, abort_flag, p.status,
+                                     81)))
                     break;
                 tc_fence_after();
-                const uint32_t acc = tmem + (uint32_t)(b * BN);
+                const uint32_t acc = tmem + (uint32_t)(b * C::HALVES * BN);
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     if (!(ok = mbar_wait(gbar(bars->full[s]), (it / C::STAGES) & 1, abort_flag, p.status, 82)))
@@ -184,7 +196,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint64_t da = da0 + s * kStage, db = db0 + s * kStage;
 #pragma unroll
                     for (int kk = 0; kk < GBK / 16; ++kk)
-                        umma_ss(acc, da + kk * kStep, db + kk * kStepB, idesc, (kb | kk) ? 1u : 0u);
+#pragma unroll
+                        for (int h = 0; h < C::HALVES; ++h)
+                            umma_ss(acc + (uint32_t)(h * BN), da + h * (C::A_HALF >> 4) + kk * kStep,
+                                    db + kk * kStepB, idesc, (kb | kk) ? 1u : 0u);
                     umma_commit(gbar(bars->empty[s]));
                 }
                 if (ok) umma_commit(gbar(bars->acc_full[b]));
@@ -195,24 +210,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         __syncwarp();
     } else if (warp >= 4) {
         // ------------------------------------------------------------ epilogue
-        const int wi = warp - 4;
-        const int row = wi * 32 + lane;
-        const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
+        const int half = (warp - 4) / 4;  // which 128-row half of the tile
+        const int wi = warp % 4;          // TMEM lane quadrant of this warp
+        const int row = half * 128 + wi * 32 + lane;
+        const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16) + (uint32_t)(half * BN);
         const bool vec_ok = (p.ldc % 8 == 0) && (p.r == nullptr || p.ldr % 8 == 0);
         int lt = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++lt) {
-            const int b = lt & 1;
-            if (!mbar_wait(gbar(bars->acc_full[b]), (lt >> 1) & 1, abort_flag, p.status, 83)) break;
+            const int b = lt % C::NBUF;
+            if (!mbar_wait(gbar(bars->acc_full[b]), (lt / C::NBUF) & 1, abort_flag, p.status, 83)) break;
             tc_fence_after();
             int mt, nt;
             tile_coords(t, p.tiles_m, p.tiles_n, mt, nt);
-            const int m = mt * GBM + row;
+            const int m = mt * BM + row;
             const bool row_ok = m < p.M;
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 uint32_t v[32];
                 __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the guarded stores
-                tmem_ld32(tl + (uint32_t)(b * BN + c), v);
+                tmem_ld32(tl + (uint32_t)(b * C::HALVES * BN + c), v);
                 tmem_ld_wait();
                 reg_fence<32>(v);
                 const int n0 = nt * BN + c;
@@ -278,20 +294,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
     if (warp == 2) {
         tc_fence_after();
-        tmem_dealloc(tmem, 2 * BN);
+        tmem_dealloc(tmem, C::TMEM_COLS);
     }
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BM, int BN, bool A_MN, bool B_MN>
 cudaError_t launch_gemm(cudaStream_t st, int sm_count, const CUtensorMap& ta, const CUtensorMap& tb,
                         const GemmParams& p) {
-    using C = GCfg<BN>;
-    auto kern = gemm_bf16_kernel<BN, A_MN, B_MN>;
+    using C = GCfg<BM, BN>;
+    auto kern = gemm_bf16_kernel<BM, BN, A_MN, B_MN>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     const int tiles = p.tiles_m * p.tiles_n;
     const int grid = tiles < sm_count ? tiles : sm_count;
-    kern<<<grid, kGemmThreads, C::SMEM, st>>>(ta, tb, p);
+    kern<<<grid, C::THREADS, C::SMEM, st>>>(ta, tb, p);
     note_launch();
     return cudaGetLastError();
 }
@@ -317,18 +333,24 @@ bool gemm_bf16_supported(bool a_mn, bool b_mn, int M, int N, int K, const void* 
 
 cudaError_t gemm_bf16(cudaStream_t st, int sm_count, DeviceStatus* status, bool a_mn, bool b_mn, int M, int N,
                       int K, const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
-                      const void* R, int64_t ldr, const void* bias) {
+                      const void* R, int64_t ldr, const void* bias, int tile) {
     if (!gemm_bf16_supported(a_mn, b_mn, M, N, K, A, lda, B, ldb, C, ldc, R, ldr, bias))
         return cudaErrorNotSupported;
-    const int tiles_m = (M + GBM - 1) / GBM;
-    const int t128 = tiles_m * ((N + 127) / 128), t256 = tiles_m * ((N + 255) / 256);
-    // BN = 256 halves the B-operand traffic per FLOP; BN = 128 when it fills
-    // the last wave of SMs clearly better.
-    const bool wide = N > 128 && wave_fill(t256, sm_count) + 0.1 >= wave_fill(t128, sm_count);
-    const int BN = wide ? 256 : 128;
+    // Tile shape: 256 x 256 reads the least operand data per FLOP (the kernel
+    // is L2-bandwidth bound at small K) but exposes its epilogue once per tile
+    // and fills waves coarsely; 128 x 256 overlaps the epilogue; 128 x 128
+    // serves narrow outputs. `tile` (1, 2, 3) forces one of them.
+    auto tiles_of = [&](int bm, int bn) { return ((M + bm - 1) / bm) * ((N + bn - 1) / bn); };
+    int BM = 128, BN = N > 128 ? 256 : 128;
+    if (tile == 0 && N > 128 && M > 128 && tiles_of(256, 256) >= 2 * sm_count &&
+        wave_fill(tiles_of(256, 256), sm_count) >= 0.85)
+        BM = 256;
+    if (tile == 1) BM = 128, BN = 128;
+    if (tile == 2) BM = 128, BN = 256;
+    if (tile == 3) BM = 256, BN = 256;
     CUtensorMap ta, tb;
     const bool ok_a = a_mn ? make_tmap_2d_ld(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 64, 64)
-                           : make_tmap_2d_ld(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, GBM);
+                           : make_tmap_2d_ld(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, 128);
     const bool ok_b = b_mn ? make_tmap_2d_ld(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, 64)
                            : make_tmap_2d_ld(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BN);
     if (!ok_a || !ok_b) return cudaErrorInvalidValue;
@@ -341,17 +363,18 @@ cudaError_t gemm_bf16(cudaStream_t st, int sm_count, DeviceStatus* status, bool 
     p.M = M;
     p.N = N;
     p.K = K;
-    p.tiles_m = tiles_m;
+    p.tiles_m = (M + BM - 1) / BM;
     p.tiles_n = (N + BN - 1) / BN;
     p.status = status;
-#define HX_GEMM_CASE(bn, amn, bmn) \
-    if (BN == bn && a_mn == amn && b_mn == bmn) return launch_gemm<bn, amn, bmn>(st, sm_count, ta, tb, p);
-    HX_GEMM_CASE(256, false, true)
-    HX_GEMM_CASE(256, false, false)
-    HX_GEMM_CASE(256, true, true)
-    HX_GEMM_CASE(128, false, true)
-    HX_GEMM_CASE(128, false, false)
-    HX_GEMM_CASE(128, true, true)
+#define HX_GEMM_CASE(bm, bn, amn, bmn)                     \
+    if (BM == bm && BN == bn && a_mn == amn && b_mn == bmn) \
+        return launch_gemm<bm, bn, amn, bmn>(st, sm_count, ta, tb, p);
+#define HX_GEMM_SHAPES(amn, bmn) \
+    HX_GEMM_CASE(256, 256, amn, bmn) HX_GEMM_CASE(128, 256, amn, bmn) HX_GEMM_CASE(128, 128, amn, bmn)
+    HX_GEMM_SHAPES(false, true)
+    HX_GEMM_SHAPES(false, false)
+    HX_GEMM_SHAPES(true, true)
+#undef HX_GEMM_SHAPES
 #undef HX_GEMM_CASE
     return cudaErrorNotSupported;  // (A MN-major, B K-major) is not a Linear product
 }

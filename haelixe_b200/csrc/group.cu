@@ -248,9 +248,25 @@ int check_flags(int flags) {
     return (flags & ~known) ? HX_ERR_INVALID : HX_OK;
 }
 
+// Waits for the member's side stream, but never for longer than the group's
+// timeout: a gather whose peer never came is aborted first (its kernel then
+// returns), so tearing a group down cannot hang.
+void drain_member(hx_group* g, hx_group_member& m) {
+    if (!m.stream) return;
+    const auto dl = deadline_of(g);
+    while (cudaStreamQuery(m.stream) == cudaErrorNotReady) {
+        if (Clock::now() > dl) {
+            abort_all(g);
+            break;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
+    cudaStreamSynchronize(m.stream);
+}
+
 void release_member(const NcclApi* a, hx_group* g, hx_group_member& m) {
     DeviceGuard dg(m.device >= 0 ? m.device : 0);
-    if (m.stream) cudaStreamSynchronize(m.stream);
+    drain_member(g, m);
     if (a && m.comm && !g->aborted) {
         if (m.win && a->CommWindowDeregister) a->CommWindowDeregister(m.comm, m.win);
         if (m.reg) a->CommDeregister(m.comm, m.reg);
@@ -273,7 +289,8 @@ int ensure_buffer(hx_group* g, hx_group_member& m, uint64_t slot) {
     const NcclApi* a = nccl();
     DeviceGuard dg(m.device);
     if (m.buf) {
-        cudaStreamSynchronize(m.stream);
+        drain_member(g, m);
+        if (g->aborted) return gfail(g, HX_ERR_NCCL, "the group was aborted");
         if (m.win && a->CommWindowDeregister) a->CommWindowDeregister(m.comm, m.win);
         if (m.reg) a->CommDeregister(m.comm, m.reg);
         a->MemFree(m.buf);
@@ -540,7 +557,7 @@ int hx_group_sync(hx_group* g, int member) {
         if (Clock::now() > dl) {
             abort_all(g);
             // The aborted communicator's kernels return; drain the side stream.
-            cudaStreamSynchronize(m.stream);
+            drain_member(g, m);
             m.pending = false;
             return gfail(g, HX_ERR_NCCL, "all-gather (rank %d) did not complete within %d ms (a peer has left "
                          "or stalled); communicator aborted", m.rank, g->timeout_ms);

@@ -599,12 +599,13 @@ static int rope_table_for(hx_ctx* c, const hx_attn_shape* shape, float base, flo
 }
 
 static int rope_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* x,
-                       void* out, float base, float sign, const char* who) {
+                       void* out, float base, float sign, const char* who, const void* x2 = nullptr,
+                       void* out2 = nullptr, bool pair = false) {
     if (c == nullptr) return HX_ERR_INVALID;
     int st;
     if ((st = validate_dtype(c, dt, who)) || (st = validate_shape(c, shape, who))) return st;
     if (empty_shape(shape)) return HX_OK;
-    if (!x || !out) return set_error(c, HX_ERR_INVALID, "%s: NULL operand", who);
+    if (!x || !out || (pair && (!x2 || !out2))) return set_error(c, HX_ERR_INVALID, "%s: NULL operand", who);
     if (shape->D % 2) return set_error(c, HX_ERR_INVALID, "%s: head_dim must be even", who);
     if (!isfinite(base) || base <= 0.f)
         return set_error(c, HX_ERR_INVALID, "%s: base must be positive and finite", who);
@@ -613,8 +614,14 @@ static int rope_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const
     LaunchCount lc(c);
     float2* tab = nullptr;
     if ((st = rope_table_for(c, shape, base, &tab, who))) return st;
-    return check_cuda(c, hx::rope_apply(c->stream, c->sm_count, dt, hx::dims_of(*shape), x, out, tab, sign),
+    return check_cuda(c, hx::rope_apply(c->stream, c->sm_count, dt, hx::dims_of(*shape), x, out, tab, sign, x2,
+                                        out2),
                       who);
+}
+
+int hx_rope_fwd_qk(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* q, const void* k,
+                   void* q_out, void* k_out, float base) {
+    return rope_common(c, dt, shape, q, q_out, base, 1.f, "hx_rope_fwd_qk", k, k_out, true);
 }
 
 int hx_rope_fwd(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, const void* x, void* out,
@@ -688,11 +695,12 @@ static int gemm_tc(hx_ctx* c, hx_dtype dt, bool a_mn, bool b_mn, int m, int n, i
                    const void* B, int ldb, void* C, int ldc, const void* R, const void* bias, const char* who,
                    bool* done) {
     *done = false;
-    if (dt != HX_BF16 || c->gemm_backend != 0 ||
+    if (dt != HX_BF16 || c->gemm_backend == 1 ||
         !hx::gemm_bf16_supported(a_mn, b_mn, m, n, k, A, lda, B, ldb, C, ldc, R, ldc, bias))
         return HX_OK;
     const int st = check_cuda(c, hx::gemm_bf16(c->stream, c->sm_count, c->status, a_mn, b_mn, m, n, k, A, lda, B,
-                                               ldb, C, ldc, R, ldc, bias),
+                                               ldb, C, ldc, R, ldc, bias,
+                                               c->gemm_backend >= 2 ? c->gemm_backend - 1 : 0),
                               who);
     if (st == HX_OK) {
         *done = true;
@@ -984,7 +992,7 @@ int hx_selftest_wait_timeout(hx_ctx* c) {
 int hx_last_gemm_path(const hx_ctx* c) { return c ? c->last_gemm_path : 0; }
 
 int hx_set_gemm_backend(hx_ctx* c, int backend) {
-    if (c == nullptr || (backend != 0 && backend != 1)) return HX_ERR_INVALID;
+    if (c == nullptr || backend < 0 || backend > 4) return HX_ERR_INVALID;
     c->gemm_backend = backend;
     return HX_OK;
 }

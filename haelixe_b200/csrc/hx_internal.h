@@ -56,7 +56,9 @@ struct hx_ctx {
     std::vector<hx::RopeTable> rope_tables;  // (cos, sin) tables, freed with the context
     std::mutex blas_mu;
     void* blas = nullptr;  // cublasHandle_t for the f32 Linear GEMMs, created on first use
-    int gemm_backend = 0;  // bf16 Linear GEMMs: 0 = tcgen05 kernel where it applies, 1 = cuBLAS
+    // bf16 Linear GEMMs: 0 = tcgen05 kernel where it applies (tile from the
+    // shape), 1 = cuBLAS, 2/3/4 = tcgen05 with tiles 128x128 / 128x256 / 256x256
+    int gemm_backend = 0;
     int last_gemm_path = 0;  // 1 cuBLAS, 2 tcgen05 (the last Linear GEMM of this context)
 };
 
@@ -129,9 +131,10 @@ cudaError_t selftest_wait_timeout(cudaStream_t st, DeviceStatus* status);
 // when the operands do not meet TMA's layout rules (the caller uses cuBLAS).
 bool gemm_bf16_supported(bool a_mn, bool b_mn, int M, int N, int K, const void* A, int64_t lda, const void* B,
                          int64_t ldb, const void* C, int64_t ldc, const void* R, int64_t ldr, const void* bias);
+// tile: 0 = chosen from the shape, 1 = 128 x 128, 2 = 128 x 256, 3 = 256 x 256.
 cudaError_t gemm_bf16(cudaStream_t st, int sm_count, DeviceStatus* status, bool a_mn, bool b_mn, int M, int N,
                       int K, const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
-                      const void* R, int64_t ldr, const void* bias);
+                      const void* R, int64_t ldr, const void* bias, int tile = 0);
 
 // ---- head reassembly (heads.cu) ----
 cudaError_t reassemble_heads(cudaStream_t st, int elem_bytes, const void* src, void* dst, int n,
@@ -144,7 +147,9 @@ uint64_t launches_of_this_thread();
 // ---- RoPE (rope.cu) ----
 // Fills tab[S][D/2] with (cos, sin) of s * inv_freq[i].
 cudaError_t rope_table(cudaStream_t st, int S, int D, const float* inv_freq_host, float2* tab);
+// With x2/out2: a second tensor of the same shape and strides in the same launch.
 cudaError_t rope_apply(cudaStream_t st, int sm_count, hx_dtype dt, const AttnDims& d,
-                       const void* x, void* out, const float2* tab, float sign);
+                       const void* x, void* out, const float2* tab, float sign, const void* x2 = nullptr,
+                       void* out2 = nullptr);
 
 }  // namespace hx

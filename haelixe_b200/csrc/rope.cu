@@ -51,14 +51,23 @@ __device__ __forceinline__ I mod_by(I x, I v, int k) { return k >= 0 ? (x & (v -
 // element strides; D % 8 == 0 on this path. I is the index type: 32-bit
 // when the host has checked that the index space and one grid stride fit,
 // else 64-bit. gk, sk, hk: log2 of D/8, S, H, or -1 when not a power of two.
+// x2/out2 (optional): a second tensor of the same shape and strides, rotated
+// in the same launch (Q and K before attention): its index space follows the
+// first one's.
 template <typename T, typename I>
-__global__ void __launch_bounds__(256) rope_kernel8(const T* x, T* out, const float2* __restrict__ tab,
-                                                    AttnDims d, float sign, int gk, int sk, int hk) {
+__global__ void __launch_bounds__(256) rope_kernel8(const T* x, T* out, const T* x2, T* out2,
+                                                    const float2* __restrict__ tab, AttnDims d, float sign,
+                                                    int gk, int sk, int hk) {
     const int half = d.D / 2;
     const I groups = (I)(d.D / 8), S = (I)d.S, H = (I)d.H;
-    const I total = (I)d.B * H * S * groups;
+    const I total1 = (I)d.B * H * S * groups;
+    const I total = x2 ? 2 * total1 : total1;
     const I stride = (I)gridDim.x * (I)blockDim.x;
-    for (I idx = (I)blockIdx.x * (I)blockDim.x + (I)threadIdx.x; idx < total; idx += stride) {
+    for (I idx0 = (I)blockIdx.x * (I)blockDim.x + (I)threadIdx.x; idx0 < total; idx0 += stride) {
+        const bool second = idx0 >= total1;
+        const I idx = second ? idx0 - total1 : idx0;
+        const T* src = second ? x2 : x;
+        T* dst = second ? out2 : out;
         const int g = (int)mod_by(idx, groups, gk);
         I r = div_by(idx, groups, gk);
         const int s = (int)mod_by(r, S, sk);
@@ -72,7 +81,7 @@ __global__ void __launch_bounds__(256) rope_kernel8(const T* x, T* out, const fl
                               make_float2(c23.x, c23.y), make_float2(c23.z, c23.w)};
         float v[8], y[8];
         if constexpr (sizeof(T) == 2) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(x + off);
+            const uint4 raw = *reinterpret_cast<const uint4*>(src + off);
             const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -81,8 +90,8 @@ __global__ void __launch_bounds__(256) rope_kernel8(const T* x, T* out, const fl
                 v[2 * k + 1] = f.y;
             }
         } else {
-            const float4 a = *reinterpret_cast<const float4*>(x + off);
-            const float4 c = *reinterpret_cast<const float4*>(x + off + 4);
+            const float4 a = *reinterpret_cast<const float4*>(src + off);
+            const float4 c = *reinterpret_cast<const float4*>(src + off + 4);
             v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
             v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
         }
@@ -93,10 +102,10 @@ __global__ void __launch_bounds__(256) rope_kernel8(const T* x, T* out, const fl
             __nv_bfloat162* q2 = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
             for (int k = 0; k < 4; ++k) q2[k] = __floats2bfloat162_rn(y[2 * k], y[2 * k + 1]);
-            *reinterpret_cast<uint4*>(out + off) = o;
+            *reinterpret_cast<uint4*>(dst + off) = o;
         } else {
-            *reinterpret_cast<float4*>(out + off) = make_float4(y[0], y[1], y[2], y[3]);
-            *reinterpret_cast<float4*>(out + off + 4) = make_float4(y[4], y[5], y[6], y[7]);
+            *reinterpret_cast<float4*>(dst + off) = make_float4(y[0], y[1], y[2], y[3]);
+            *reinterpret_cast<float4*>(dst + off + 4) = make_float4(y[4], y[5], y[6], y[7]);
         }
     }
 }
@@ -137,11 +146,17 @@ __global__ void __launch_bounds__(256) rope_kernel1(const T* x, T* out, const fl
 
 template <typename T>
 cudaError_t launch_rope(cudaStream_t st, int sm_count, const AttnDims& d, const void* x, void* out,
-                        const float2* tab, float sign) {
+                        const float2* tab, float sign, const void* x2 = nullptr, void* out2 = nullptr) {
     const int eb = (int)sizeof(T);
     const bool vec = d.D % 8 == 0 && ((uintptr_t)x % 16 == 0) && ((uintptr_t)out % 16 == 0) &&
                      (d.ss * eb) % 16 == 0 && (d.sh * eb) % 16 == 0 && (d.sb * eb) % 16 == 0;
-    const int64_t work = (int64_t)d.B * d.H * d.S * (vec ? d.D / 8 : d.D / 2);
+    if (x2 != nullptr) {  // one launch for both tensors: the vector kernel only
+        if (!vec || (uintptr_t)x2 % 16 || (uintptr_t)out2 % 16) {
+            cudaError_t e = launch_rope<T>(st, sm_count, d, x, out, tab, sign);
+            return e != cudaSuccess ? e : launch_rope<T>(st, sm_count, d, x2, out2, tab, sign);
+        }
+    }
+    const int64_t work = (int64_t)d.B * d.H * d.S * (vec ? d.D / 8 : d.D / 2) * (x2 ? 2 : 1);
     int64_t blocks = (work + 255) / 256;
     const int64_t cap = (int64_t)sm_count * 16;
     if (blocks > cap) blocks = cap;
@@ -149,10 +164,11 @@ cudaError_t launch_rope(cudaStream_t st, int sm_count, const AttnDims& d, const 
     auto log2_of = [](int64_t v) { return (v > 0 && (v & (v - 1)) == 0) ? __builtin_ctzll((uint64_t)v) : -1; };
     const int gk = log2_of(d.D / 8), sk = log2_of(d.S), hk = log2_of(d.H);
     if (vec && work + blocks * 256 < (int64_t(1) << 32))
-        rope_kernel8<T, uint32_t><<<(unsigned)blocks, 256, 0, st>>>((const T*)x, (T*)out, tab, d, sign, gk, sk,
-                                                                  hk);
+        rope_kernel8<T, uint32_t><<<(unsigned)blocks, 256, 0, st>>>((const T*)x, (T*)out, (const T*)x2, (T*)out2,
+                                                                  tab, d, sign, gk, sk, hk);
     else if (vec)
-        rope_kernel8<T, int64_t><<<(unsigned)blocks, 256, 0, st>>>((const T*)x, (T*)out, tab, d, sign, gk, sk, hk);
+        rope_kernel8<T, int64_t><<<(unsigned)blocks, 256, 0, st>>>((const T*)x, (T*)out, (const T*)x2, (T*)out2,
+                                                                 tab, d, sign, gk, sk, hk);
     else
         rope_kernel1<T><<<(unsigned)blocks, 256, 0, st>>>((const T*)x, (T*)out, tab, d, sign);
     note_launch();
@@ -173,9 +189,9 @@ cudaError_t rope_table(cudaStream_t st, int S, int D, const float* inv_freq_host
 }
 
 cudaError_t rope_apply(cudaStream_t st, int sm_count, hx_dtype dt, const AttnDims& d,
-                       const void* x, void* out, const float2* tab, float sign) {
-    if (dt == HX_F32) return launch_rope<float>(st, sm_count, d, x, out, tab, sign);
-    return launch_rope<__nv_bfloat16>(st, sm_count, d, x, out, tab, sign);
+                       const void* x, void* out, const float2* tab, float sign, const void* x2, void* out2) {
+    if (dt == HX_F32) return launch_rope<float>(st, sm_count, d, x, out, tab, sign, x2, out2);
+    return launch_rope<__nv_bfloat16>(st, sm_count, d, x, out, tab, sign, x2, out2);
 }
 
 }  // namespace hx

@@ -220,6 +220,11 @@ int hx_rope_fwd(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape, const v
                 float base);
 int hx_rope_bwd(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape, const void* g, void* out,
                 float base);
+/* Q and K (same shape and strides) rotated as hx_rope_fwd does, in one
+ * launch: the two rotations that precede the attention
+ * (src/nn/attention.rs:76-78). Each output may alias its input. */
+int hx_rope_fwd_qk(hx_ctx* ctx, hx_dtype dtype, const hx_attn_shape* shape, const void* q, const void* k,
+                   void* q_out, void* k_out, float base);
 
 /* ---- the attention block around the kernel (src/nn/attention.rs:46-98) ------------ */
 /* y[rows, out] = x[rows, in] w[in, out] + b[out] (Linear::forward,
@@ -377,8 +382,9 @@ int hx_set_force_simt(hx_ctx* ctx, int force);
 /* Which GEMM ran the last Linear product on this context: 0 none, 1 cuBLAS,
  * 2 the tcgen05 kernel. */
 int hx_last_gemm_path(const hx_ctx* ctx);
-/* bf16 Linear GEMMs: 0 = the tcgen05 kernel where it applies (default),
- * 1 = always cuBLAS. */
+/* bf16 Linear GEMMs: 0 = the tcgen05 kernel where it applies, its tile
+ * chosen from the shape (default); 1 = always cuBLAS; 2, 3, 4 = the tcgen05
+ * kernel with 128x128, 128x256 or 256x256 output tiles. */
 int hx_set_gemm_backend(hx_ctx* ctx, int backend);
 /* Exercises the kernels' failure path: enqueues one CTA whose bounded
  * mbarrier wait can never complete. After the wait limit (2 s) it records the

@@ -148,6 +148,23 @@ def test_rope_matches_oracle(dtype, base):
     assert np.max(np.abs(z.float().cpu().numpy() - refz)) < tol
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
+@pytest.mark.parametrize("shape", [(2, 3, 257, 128), (1, 4, 1024, 64), (2, 2, 33, 40)])
+def test_rope_qk_one_launch_equals_two(shape, dtype):
+    """hx_rope_fwd_qk rotates Q and K exactly as two hx_rope_fwd calls do
+    (one launch; layouts the vector kernel cannot take run as two)."""
+    q = torch.from_numpy(_host(shape, 31, dtype)).to(dtype).cuda()
+    k = torch.from_numpy(_host(shape, 32, dtype)).to(dtype).cuda()
+    ctx = hx.context()
+    ref_q, ref_k = hx.rope_forward(q, 500000.0), hx.rope_forward(k, 500000.0)  # also builds the table
+    n0 = N.lib().hx_kernel_launches(ctx.handle)
+    qr, kr = hx.rope_forward_qk(q, k, 500000.0)
+    n1 = N.lib().hx_kernel_launches(ctx.handle)
+    assert torch.equal(qr, ref_q) and torch.equal(kr, ref_k)
+    if shape[-1] % 8 == 0:
+        assert n1 - n0 == 1
+
+
 def test_arena_bins_and_reuse():
     ctx = hx.CudaContext(0)
     try:

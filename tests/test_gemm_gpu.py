@@ -108,3 +108,29 @@ def test_layouts_the_kernel_refuses_fall_back_to_cublas():
     NA.check(L.hx_linear_fwd(ctx.handle, NA.HX_BF16, _p(x), _p(w), _p(b), _p(y), M, K, N_), ctx.handle)
     assert L.hx_last_gemm_path(ctx.handle) == CUBLAS
     _close(y, x.float() @ w.float() + b.float(), "y")
+
+
+@pytest.mark.parametrize("tile", [2, 3, 4], ids=["128x128", "128x256", "256x256"])
+@pytest.mark.parametrize("M,K,N", [(300, 200, 136), (1000, 512, 384), (520, 64, 264), (2048, 1024, 2048)])
+def test_every_tile_shape(M, K, N, tile):
+    """Each tile configuration (forced with hx_set_gemm_backend) on ragged and whole shapes."""
+    L = NA.lib()
+    ctx = hx.context(0)
+    ctx.use_stream()
+    x, w, b, r, dy = _data(M, K, N, 3 * M + K + N + tile)
+    try:
+        NA.check(L.hx_set_gemm_backend(ctx.handle, tile), ctx.handle)
+        y = r.clone()
+        NA.check(L.hx_linear_residual_fwd(ctx.handle, NA.HX_BF16, _p(x), _p(w), _p(b), _p(y), _p(y), M, K, N),
+                 ctx.handle)
+        assert L.hx_last_gemm_path(ctx.handle) == TCGEN05
+        dx, dw = torch.empty_like(x), torch.empty_like(w)
+        NA.check(L.hx_linear_bwd(ctx.handle, NA.HX_BF16, _p(x), _p(w), _p(dy), _p(dx), _p(dw), None, M, K, N),
+                 ctx.handle)
+    finally:
+        NA.check(L.hx_set_gemm_backend(ctx.handle, 0), ctx.handle)
+    torch.cuda.synchronize()
+    xf, wf = x.float(), w.float()
+    _close(y, r.float() + (xf @ wf + b.float()), "y + residual")
+    _close(dx, dy.float() @ wf.t(), "dx")
+    _close(dw, xf.t() @ dy.float(), "dw")
