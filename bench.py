@@ -90,6 +90,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--workload", choices=["attention", "block_stack"], default="attention")
+    p.add_argument("--gemm-backend", choices=["tcgen05", "cublas"], default="tcgen05",
+                   help="block_stack workload: the bf16 Linear GEMMs on this library's kernel or on cuBLAS")
     p.add_argument("--rope-launches", type=int, choices=[1, 2], default=2,
                    help="rotate Q and K in two launches (hx_rope_fwd) or in one (hx_rope_fwd_qk)")
     p.add_argument("--exchange-flags", type=int, default=0,
@@ -564,6 +566,7 @@ def run_block_stack(a):
     params = model.parameters()
     opt = hx.optim.AdamW(1e-4)
     ctx = hx.context(local)
+    N.check(N.lib().hx_set_gemm_backend(ctx.handle, 1 if a.gemm_backend == "cublas" else 0), ctx.handle)
     g = torch.Generator().manual_seed(a.seed)
     ids_h = torch.randint(0, V, (B, S), generator=g, dtype=torch.int32).pin_memory()
     tgt_h = torch.randint(0, V, (B * S,), generator=g, dtype=torch.int32).pin_memory()
@@ -609,6 +612,7 @@ def run_block_stack(a):
         "config": {"workload": f"{L}-block TransformerBlock LM d{Hd} H{H}x{Hd // H} MLP {4 * Hd} vocab {V} "
                                f"B{B} S{S} causal, bf16 + f32 master, AdamW",
                    "parameters": int(sum(q.numel() for q in params)),
+                   "gemm": a.gemm_backend,
                    "l2": "activations and weights far larger than L2"},
         "model_tflops": flops / (ms * 1e-3) / 1e12, "flops_per_step": flops,
         "loss_warmup": losses, "loss": float(loss_h.item()),

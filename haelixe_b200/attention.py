@@ -136,6 +136,11 @@ def _shape_of(t: torch.Tensor) -> N.AttnShape:
     raise ValueError(f"attention operands are [BH,S,D] or [B,H,S,D], got {tuple(t.shape)}")
 
 
+def _same_strides(a: torch.Tensor, b: torch.Tensor) -> bool:
+    # The stride of a dimension of size 1 never moves an address, so it may differ.
+    return all(n == 1 or x == y for n, x, y in zip(a.shape, a.stride(), b.stride()))
+
+
 def _check_operands(*ts: torch.Tensor) -> None:
     t0 = ts[0]
     for t in ts:
@@ -148,7 +153,7 @@ def _check_operands(*ts: torch.Tensor) -> None:
             raise ValueError("q, k, v (and gradients) must share dtype, shape and device")
         if t.stride(-1) != 1:
             raise ValueError("the head dimension must be contiguous")
-        if t.dim() == 4 and (t.stride() != t0.stride()):
+        if t.dim() == 4 and not _same_strides(t, t0):
             raise ValueError("strided operands must share strides")
 
 
@@ -160,7 +165,7 @@ def _like(t: torch.Tensor) -> torch.Tensor:
 
 def _check_outputs(ref: torch.Tensor, *outs: Optional[torch.Tensor]) -> None:
     for t in outs:
-        if t is not None and (t.shape != ref.shape or t.stride() != ref.stride() or t.dtype != ref.dtype
+        if t is not None and (t.shape != ref.shape or not _same_strides(t, ref) or t.dtype != ref.dtype
                               or t.device != ref.device):
             raise ValueError("output tensors must have the inputs' shape, strides, dtype and device")
 
@@ -194,7 +199,7 @@ def attn_backward(q, k, v, o, lse, dout, scale: float, causal: bool = False,
     dq, dk are returned with respect to the tensors before the rotation
     (rope_backward fused into the backward's last writes of dq and dk).
     """
-    if dout.stride() != q.stride():  # e.g. a contiguous upstream gradient of a strided view
+    if not _same_strides(dout, q):  # e.g. a contiguous upstream gradient of a strided view
         dout = _like(q).copy_(dout)
     _check_operands(q, k, v, o, dout)
     ctx = context(q.device.index)
@@ -294,7 +299,7 @@ def rope_forward_qk(q: torch.Tensor, k: torch.Tensor, base: float, out_q: Option
                     out_k: Optional[torch.Tensor] = None):
     """rope_forward of q and k (same shape and strides) in one launch."""
     _check_operands(q, k)
-    if q.shape != k.shape or q.stride() != k.stride():
+    if q.shape != k.shape or not _same_strides(q, k):
         raise ValueError("q and k must have the same shape and strides")
     ctx = context(q.device.index)
     ctx.use_stream()
@@ -302,7 +307,7 @@ def rope_forward_qk(q: torch.Tensor, k: torch.Tensor, base: float, out_q: Option
     _check_outputs(k, out_k)
     out_q = _like(q) if out_q is None else out_q
     out_k = _like(k) if out_k is None else out_k
-    if out_q.stride() != q.stride() or out_k.stride() != k.stride():
+    if not (_same_strides(out_q, q) and _same_strides(out_k, k)):
         raise ValueError("outputs must have the strides of the inputs")
     shp = _shape_of(q)
     N.check(N.lib().hx_rope_fwd_qk(ctx.handle, _DTYPES[q.dtype], ctypes.byref(shp), _ptr(q), _ptr(k),
