@@ -94,6 +94,10 @@ def parse():
                    help="block_stack workload: the bf16 Linear GEMMs on this library's kernel or on cuBLAS")
     p.add_argument("--rope-launches", type=int, choices=[1, 2], default=2,
                    help="rotate Q and K in two launches (hx_rope_fwd) or in one (hx_rope_fwd_qk)")
+    p.add_argument("--head-layout", choices=["bhsd", "bshd"], default="bhsd",
+                   help="memory of Q, K, V, dO, O and the gradients: [B, H, S, D], or [B, S, H, D] (the "
+                        "projection rows of the multi-head layer, heads as strided views); with N > 1 the "
+                        "latter lets the head merge run as copy-engine copies")
     p.add_argument("--exchange-flags", type=int, default=0,
                    help="hx_group flags of the N>1 exchange: 1 register, 2 symmetric window, 4 copy engines")
     return p.parse_args()
@@ -114,7 +118,7 @@ def config_of(a, n):
     return {
         "workload": workload_name(a),
         "batch": a.batch, "heads": a.heads, "seq_len": a.seq, "head_dim": a.head_dim,
-        "causal": not a.no_causal, "rope_theta": a.rope_theta,
+        "causal": not a.no_causal, "rope_theta": a.rope_theta, "head_layout": a.head_layout,
         "parallelism": f"heads/{n} per GPU + NCCL all-gather of O" if n > 1 else "1 GPU, all heads",
         "l2": ("inputs larger than L2 (each operand %.0f MB > 126 MB)" if op_mb > 126 else
                "inputs smaller than L2 (each operand %.0f MB); no L2 flush") % op_mb,
@@ -327,7 +331,10 @@ def run_haelixe(a):
     # Inputs for this rank's heads, generated from the global head index so a
     # head's data does not depend on the GPU count.
     def gen(which):
-        t = torch.empty(B, Hl, S, D, device=dev, dtype=torch.bfloat16)
+        if a.head_layout == "bshd":
+            t = torch.empty(B, S, Hl, D, device=dev, dtype=torch.bfloat16).permute(0, 2, 1, 3)
+        else:
+            t = torch.empty(B, Hl, S, D, device=dev, dtype=torch.bfloat16)
         for hl in range(Hl):
             g = torch.Generator(device=dev).manual_seed(a.seed * 1000003 + which * 1009 + rank * Hl + hl)
             t[:, hl] = torch.randn(B, S, D, device=dev, generator=g).to(torch.bfloat16)
@@ -346,7 +353,8 @@ def run_haelixe(a):
         # The forward writes O straight into this rank's slot of the group's
         # gather buffer, so the all-gather runs in place.
         gbuf = group.gather_buffer((B, Hl, S, D), torch.bfloat16)
-        bufs0["o"] = gbuf[rank]
+        bufs0["o"] = (gbuf[rank].view(B, S, Hl, D).permute(0, 2, 1, 3) if a.head_layout == "bshd"
+                      else gbuf[rank])
         merged = torch.empty(B, S, H, D, device=dev, dtype=torch.bfloat16)
     qr, kr, o, lse = bufs0["qr"], bufs0["kr"], bufs0["o"], bufs0["lse"]
     dv, dq0, dk0 = bufs0["dv"], bufs0["dq0"], bufs0["dk0"]

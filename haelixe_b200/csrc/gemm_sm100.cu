@@ -353,7 +353,8 @@ cudaError_t gemm_bf16(cudaStream_t st, int sm_count, DeviceStatus* status, bool 
                            : make_tmap_2d_ld(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, 128);
     const bool ok_b = b_mn ? make_tmap_2d_ld(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, 64)
                            : make_tmap_2d_ld(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BN);
-    if (!ok_a || !ok_b) return cudaErrorInvalidValue;
+    if (!ok_a) return cudaErrorInvalidValue;       // the A operand's tensor map was refused
+    if (!ok_b) return cudaErrorInvalidPitchValue;  // the B operand's tensor map was refused
     GemmParams p;
     p.c = (__nv_bfloat16*)C;
     p.r = (const __nv_bfloat16*)R;

@@ -170,7 +170,7 @@ struct DeviceGuard {
     int prev = -1;
     explicit DeviceGuard(int dev) {
         cudaGetDevice(&prev);
-        if (prev != dev) cudaSetDevice(dev);
+        cudaSetDevice(dev);  // also makes the primary context current in this thread
     }
     ~DeviceGuard() {
         if (prev >= 0) cudaSetDevice(prev);
@@ -487,7 +487,7 @@ int hx_allgather_heads(hx_group* g, int member, hx_ctx* ctx, hx_dtype dtype, con
     if (ctx->device != m.device)
         return gfail(g, HX_ERR_INVALID, "context device %d is not member %d's device %d", ctx->device, member,
                      m.device);
-    if ((dtype != HX_BF16 && dtype != HX_F32) || B < 0 || Hs < 0 || S < 0 || D < 1 || (layout != 0 && layout != 1))
+    if ((dtype != HX_BF16 && dtype != HX_F32) || B < 0 || Hs < 0 || S < 0 || D < 1 || layout < 0 || layout > 2)
         return gfail(g, HX_ERR_INVALID, "hx_allgather_heads: bad dtype, shape or layout");
     const int esize = dtype == HX_BF16 ? 2 : 4;
     const uint64_t count = (uint64_t)B * Hs * S * D;
@@ -510,7 +510,19 @@ int hx_allgather_heads(hx_group* g, int member, hx_ctx* ctx, hx_dtype dtype, con
         return gfail(g, HX_ERR_NCCL, "ncclAllGather (rank %d): %s; communicator aborted", m.rank, nstr(r));
     }
     if (int st = settle(g, m, "ncclAllGather", deadline_of(g))) return st;
-    if (merged) {
+    if (merged && layout == 2) {
+        // Shards stored [B, S, H_shard, D]: rank r's slot is B*S rows of
+        // H_shard*D elements, which land in columns [r*H_shard*D, ...) of the
+        // merged [B*S, H*D] rows. One 2D copy per rank, on the copy engines.
+        const size_t w = (size_t)Hs * D * esize;
+        for (int r = 0; r < g->nranks; ++r) {
+            const cudaError_t e =
+                cudaMemcpy2DAsync((uint8_t*)merged + (size_t)r * w, w * (size_t)g->nranks,
+                                  base + (uint64_t)r * m.slot_bytes, w, w, (size_t)B * S, cudaMemcpyDeviceToDevice,
+                                  m.stream);
+            if (e != cudaSuccess) return gfail(g, HX_ERR_CUDA, "head reassembly copy: %s", cudaGetErrorString(e));
+        }
+    } else if (merged) {
         const uint64_t t0 = launches_of_this_thread();
         const cudaError_t e = reassemble_heads(m.stream, esize, base, merged, g->nranks, B, Hs, S, D, layout,
                                                ctx->sm_count);

@@ -67,7 +67,11 @@ struct DeviceGuard {
     bool ok = false;
     explicit DeviceGuard(int dev) {
         if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-        ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
+        // Always set it: cudaSetDevice also makes the device's primary context
+        // current in this thread, which the driver calls made before any
+        // runtime call (tensor-map encoding) need; a thread that has only
+        // asked for the device (e.g. an autograd worker) may have none yet.
+        ok = cudaSetDevice(dev) == cudaSuccess;
     }
     ~DeviceGuard() {
         int cur = -1;

@@ -118,13 +118,20 @@ class HeadGroup:
     def all_gather(self, shard: torch.Tensor, merged: torch.Tensor | None = None, layout: str = "bshd",
                    member: int = 0) -> torch.Tensor | None:
         """Enqueues the gather of `shard` [B, H/N, S, D] (+ the reassembly into
-        `merged`) after the work on the current stream; returns at once."""
-        if not shard.is_contiguous():
-            raise ValueError("the shard must be contiguous")
+        `merged`, [B, S, H, D] for 'bshd', [B, H, S, D] for 'bhsd') after the
+        work on the current stream; returns at once. A shard whose memory is
+        [B, S, H/N, D] (the head-split view of projection rows) gathers into a
+        'bshd' output with copy-engine copies instead of a kernel."""
         B, Hs, S, D = shard.shape
+        rows = shard.permute(0, 2, 1, 3)
+        if shard.is_contiguous():
+            lay = {"bhsd": 0, "bshd": 1}[layout]
+        elif rows.is_contiguous() and layout == "bshd":
+            lay = 2
+        else:
+            raise ValueError("the shard must be contiguous as [B, H/N, S, D] or as [B, S, H/N, D]")
         ctx = context(shard.device.index)
         ctx.use_stream()
-        lay = {"bhsd": 0, "bshd": 1}[layout]
         self._check(N.lib().hx_allgather_heads(
             self.handle, member, ctx.handle, _DTYPES[shard.dtype], ctypes.c_void_p(shard.data_ptr()),
             ctypes.c_void_p(merged.data_ptr()) if merged is not None else None, B, Hs, S, D, lay))

@@ -360,7 +360,10 @@ int hx_group_last_error(const hx_group* group, char* buf, uint64_t n);
 int hx_group_gather_buffer(hx_group* group, int member, uint64_t slot_bytes, void** base);
 /* Gathers every rank's shard [B, H_shard, S, D] (contiguous) into the gather
  * buffer and, if merged is not NULL, reassembles it as [B, H, S, D]
- * (layout 0) or [B, S, H, D] (layout 1), H = nranks * H_shard. Runs on the
+ * (layout 0) or [B, S, H, D] (layout 1), H = nranks * H_shard. Layout 2: the
+ * shard is stored [B, S, H_shard, D] (the head-split view of a projection's
+ * [B, S, H_shard*D] rows) and merged is [B, S, H, D], assembled by one 2D copy
+ * per rank on the copy engines instead of a kernel. Runs on the
  * member's own side stream, after the work already queued on ctx's stream;
  * it returns once the work is enqueued. Order later work on ctx's stream
  * after it with hx_group_wait, or block the host with hx_group_sync. */

@@ -134,3 +134,31 @@ def test_every_tile_shape(M, K, N, tile):
     _close(y, r.float() + (xf @ wf + b.float()), "y + residual")
     _close(dx, dy.float() @ wf.t(), "dx")
     _close(dw, xf.t() @ dy.float(), "dw")
+
+
+def test_gemm_from_a_thread_without_a_current_context():
+    """The autograd engine runs backward ops on its own threads: a Linear GEMM
+    whose thread has made no CUDA runtime call yet must still encode its
+    tensor maps (the entry point makes the device's context current)."""
+    import threading
+    L = NA.lib()
+    ctx = hx.context(0)
+    M, K, N_ = 512, 1024, 640
+    x, w, b, r, dy = _data(M, K, N_, 23)
+    y = torch.empty(M, N_, device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    out = {}
+
+    def run():
+        out["rc"] = L.hx_linear_fwd(ctx.handle, NA.HX_BF16, _p(x), _p(w), _p(b), _p(y), M, K, N_)
+        out["path"] = L.hx_last_gemm_path(ctx.handle)
+        out["err"] = NA.last_error(ctx.handle) if out["rc"] else ""
+
+    t = threading.Thread(target=run)
+    t.start()
+    t.join(timeout=60)
+    assert out.get("rc") == NA.HX_OK, out
+    assert out["path"] == TCGEN05
+    L.hx_sync(ctx.handle)
+    torch.cuda.synchronize()
+    _close(y, x.float() @ w.float() + b.float(), "y")

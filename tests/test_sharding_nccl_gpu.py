@@ -102,6 +102,30 @@ def test_one_rank_group_gathers_in_place():
         g.close()
 
 
+def test_one_rank_group_merges_projection_rows_with_copies():
+    """Shards stored [B, S, H, D] (heads as strided views of projection rows):
+    the merge runs as copy-engine 2D copies (layout 2) and gives the same
+    [B, S, H, D] output as the reassembly kernel."""
+    import haelixe_b200 as hx
+    from haelixe_b200.sharding import HeadGroup
+    g = HeadGroup.create_rank(0, 1, 0, HeadGroup.unique_id(), timeout_ms=30000)
+    try:
+        q, k, v, do = _inputs(torch.device("cuda", 0))
+        rows = [t.permute(0, 2, 1, 3).contiguous().permute(0, 2, 1, 3) for t in (q, k, v, do)]
+        gbuf = g.gather_buffer((B, H, S, D), torch.bfloat16)
+        o_slot = gbuf[0].view(B, S, H, D).permute(0, 2, 1, 3)
+        merged = torch.empty(B, S, H, D, device="cuda", dtype=torch.bfloat16)
+        o, dq, dk, dv = _run(*rows, hx, o_out=o_slot, between=lambda o: g.all_gather(o, merged, "bshd"))
+        g.wait()
+        torch.cuda.synchronize()
+        g.sync()
+        ref_merged, _, rdk, rdv = _reference()
+        assert torch.equal(merged.cpu(), ref_merged)
+        assert torch.equal(dk.cpu(), rdk) and torch.equal(dv.cpu(), rdv)
+    finally:
+        g.close()
+
+
 def _never_joined(q):
     from haelixe_b200.sharding import HeadGroup
     torch.cuda.set_device(0)
