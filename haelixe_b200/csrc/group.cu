@@ -31,6 +31,12 @@
 namespace hx {
 namespace {
 
+// SMs' worth of blocks the reassembly kernel may use (0 = the whole GPU). It
+// runs beside the backward, whose CTAs it displaces when they retire.
+#ifndef HX_EXCHANGE_MERGE_SMS
+#define HX_EXCHANGE_MERGE_SMS 0
+#endif
+
 // NCCL_CTA_POLICY_ZERO of NCCL 2.28 (collectives on copy engines where the
 // buffers allow it); the header this file builds against may predate it.
 constexpr int kCtaPolicyZero = 0x02;
@@ -525,7 +531,7 @@ int hx_allgather_heads(hx_group* g, int member, hx_ctx* ctx, hx_dtype dtype, con
     } else if (merged) {
         const uint64_t t0 = launches_of_this_thread();
         const cudaError_t e = reassemble_heads(m.stream, esize, base, merged, g->nranks, B, Hs, S, D, layout,
-                                               ctx->sm_count);
+                                               HX_EXCHANGE_MERGE_SMS ? HX_EXCHANGE_MERGE_SMS : ctx->sm_count);
         ctx->kernel_launches += launches_of_this_thread() - t0;
         if (e != cudaSuccess)
             return gfail(g, HX_ERR_CUDA, "head reassembly: %s", cudaGetErrorString(e));
