@@ -98,7 +98,10 @@ def parse():
                    help="memory of Q, K, V, dO, O and the gradients: [B, H, S, D], or [B, S, H, D] (the "
                         "projection rows of the multi-head layer, heads as strided views); with N > 1 the "
                         "latter lets the head merge run as copy-engine copies")
-    p.add_argument("--exchange-flags", type=int, default=0,
+    p.add_argument("--compute-priority", choices=["default", "high"], default="default",
+                   help="run the attention step on a high-priority stream, so its CTAs are scheduled "
+                        "ahead of the exchange's (N > 1)")
+    p.add_argument("--exchange-flags", type=int, default=1,
                    help="hx_group flags of the N>1 exchange: 1 register, 2 symmetric window, 4 copy engines")
     return p.parse_args()
 
@@ -313,6 +316,8 @@ def run_haelixe(a):
         raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if a.compute_priority == "high":
+        torch.cuda.set_stream(torch.cuda.Stream(device=dev, priority=-1))
     group = None
     if world > 1:
         # Control (barriers, max over ranks) over gloo on the host; the data

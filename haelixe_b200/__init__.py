@@ -21,6 +21,8 @@ from .attention import (  # noqa: F401
     rope_backward,
     rope_forward,
     rope_forward_qk,
+    torch_arena_stats,
+    use_arena_allocator,
 )
 from ._native import HxError  # noqa: F401
 from . import nn, optim  # noqa: F401

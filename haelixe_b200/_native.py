@@ -112,6 +112,9 @@ SIGNATURES = {
     "hx_rope_bwd": (_I, [_P, _I, _SHP, _P, _P, _F]),
     "hx_rope_fwd_qk": (_I, [_P, _I, _SHP, _P, _P, _P, _P, _F]),
     "hx_reassemble_heads": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _I, _I]),
+    "hx_torch_malloc": (_P, [ctypes.c_size_t, _I, _P]),
+    "hx_torch_free": (None, [_P, ctypes.c_size_t, _I, _P]),
+    "hx_torch_arena_context": (_P, [_I]),
     "hx_group_unique_id": (_I, [_P]),
     "hx_group_create_rank": (_I, [_I, _I, _I, _P, _I, _I, ctypes.POINTER(_P)]),
     "hx_group_create": (_I, [_I, ctypes.POINTER(_I), _I, _I, ctypes.POINTER(_P)]),

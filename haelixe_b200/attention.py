@@ -282,6 +282,25 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
     return o
 
 
+def use_arena_allocator() -> None:
+    """Routes every CUDA tensor this process allocates from now on through the
+    library's arena (one per device: power-of-two bins, slabs parked on free
+    and reused), as every tensor of the reference lives in its GpuMemoryArena
+    (src/gpu/arena.rs:13-145). Call it before the first CUDA allocation."""
+    alloc = torch.cuda.memory.CUDAPluggableAllocator(N.LIB_PATH, "hx_torch_malloc", "hx_torch_free")
+    torch.cuda.memory.change_current_allocator(alloc)
+
+
+def torch_arena_stats(device: int = 0) -> dict:
+    """Statistics of the arena behind use_arena_allocator() on `device`."""
+    c = N.lib().hx_torch_arena_context(device)
+    if not c:
+        raise RuntimeError("no arena for this device")
+    st = N.ArenaStats()
+    N.check(N.lib().hx_arena_stats_get(c, ctypes.byref(st)))
+    return {f: getattr(st, f) for f, _ in N.ArenaStats._fields_}
+
+
 def rope_forward(x: torch.Tensor, base: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Interleaved-pair RoPE on [BH,S,D] / [B,H,S,D] (kernels/rope.rs:5-44)."""
     _check_operands(x)

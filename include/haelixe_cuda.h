@@ -318,6 +318,19 @@ int hx_embedding_bwd(hx_ctx* ctx, hx_dtype dtype, const void* dout, const uint32
 int hx_reassemble_heads(hx_ctx* ctx, hx_dtype dtype, const void* shards, void* out, int n_shards,
                         int B, int H_shard, int S, int D, int out_layout);
 
+/* ---- the arena as a process's tensor allocator ------------------------------------ */
+/* The reference takes every tensor's device storage from its GpuMemoryArena
+ * (src/gpu/arena.rs:13-145, Tensor storage via src/storage.rs:17-26). These
+ * two functions have the signatures torch's pluggable-allocator interface
+ * calls (size, device, cudaStream_t as void*), so a Python host can route all
+ * of its CUDA tensors through one arena per device: power-of-two bins with a
+ * 512-byte floor, slabs parked on free and reused. A slab freed on one stream
+ * and reused on another waits for an event of its last use. The arena's
+ * context (for hx_arena_stats_get) is hx_torch_arena_context(device). */
+void* hx_torch_malloc(size_t size, int device, void* stream);
+void hx_torch_free(void* ptr, size_t size, int device, void* stream);
+hx_ctx* hx_torch_arena_context(int device);
+
 /* ---- the head-sharding exchange: NCCL all-gather + reassembly ------------------ */
 /* The reference runs on one device and has no collective. Its multi-head
  * layer merges the per-head outputs after the attention
