@@ -252,13 +252,21 @@ class _FlashAttentionFn(torch.autograd.Function):
         q, k = q.detach(), k.detach()
         if rope_base is not None:
             q, k = rope_forward(q, rope_base), rope_forward(k, rope_base)
-        o, lse = attn_forward(q, k, v.detach(), scale, causal)
-        fctx.op = FlashAttentionOp(q, k, v.detach(), scale, o, lse, causal, rope_base)
+        v = v.detach()
+        o, lse = attn_forward(q, k, v, scale, causal)
+        # Saved through save_for_backward, not as attributes: o is this node's
+        # own output, and holding it on the context would make a reference
+        # cycle (node -> o -> o.grad_fn = node) that only the cyclic garbage
+        # collector frees, keeping every step's q, k, v, o and lse alive.
+        fctx.save_for_backward(q, k, v, o, lse)
+        fctx.scale, fctx.causal, fctx.rope_base = scale, causal, rope_base
         return o
 
     @staticmethod
     def backward(fctx, grad_out):
-        dq, dk, dv = fctx.op.backward(grad_out)
+        q, k, v, o, lse = fctx.saved_tensors
+        op = FlashAttentionOp(q, k, v, fctx.scale, o, lse, fctx.causal, fctx.rope_base)
+        dq, dk, dv = op.backward(grad_out)
         return dq, dk, dv, None, None, None
 
 

@@ -6,7 +6,8 @@ floor, slabs parked on free and handed out again; src/gpu/arena.rs:13-145).
 A few steps of a small TransformerBlock language model (attention, Linear,
 RMSNorm, GELU, cross-entropy, AdamW) run in a fresh process with and without
 it. The losses must agree, and after the first step the arena must serve the
-loop from parked slabs: hits grow step after step while misses stop growing.
+loop from parked slabs: hits grow step after step while misses and live bytes
+stay flat (a tensor kept alive across steps would show as growth).
 Runs in child processes because torch's allocator can only be replaced before
 the first CUDA allocation.
 """
@@ -69,7 +70,8 @@ def test_training_loop_runs_from_the_arena():
     st = arena["stats"]
     print("arena stats per step:", st)
     assert st[0]["live_bytes"] > 0 and st[0]["misses"] > 0
-    # after the first step the loop is served mostly from parked slabs
-    hits = st[-1]["hits"] - st[0]["hits"]
-    misses = st[-1]["misses"] - st[0]["misses"]
-    assert hits > 3 * misses, st
+    # after the first two steps (AdamW state is created on the first) the loop
+    # is served from parked slabs: no new slabs, no growth of live bytes
+    assert st[-1]["misses"] == st[2]["misses"], st
+    assert st[-1]["live_bytes"] == st[2]["live_bytes"], st
+    assert st[-1]["hits"] > st[2]["hits"], st
