@@ -146,6 +146,7 @@ struct hx_group {
     int flags = 0;
     int timeout_ms = 0;
     bool aborted = false;
+    std::mutex abort_mu;  // members driven from several threads may give up at once
     std::vector<hx_group_member> m;
     mutable std::mutex err_mu;
     std::string last_error;
@@ -187,6 +188,7 @@ struct DeviceGuard {
 // resources are released) after a failure or a missed deadline.
 void abort_all(hx_group* g) {
     const NcclApi* a = nccl();
+    std::lock_guard<std::mutex> lk(g->abort_mu);
     if (!a || g->aborted) return;
     for (auto& m : g->m) {
         if (m.comm) {
