@@ -89,7 +89,9 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=20)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=["attention", "block_stack"], default="attention")
+    p.add_argument("--workload", choices=["attention", "block_stack", "linear"], default="attention")
+    p.add_argument("--linear-shape", default="8192,2048,8192",
+                   help="linear workload: rows,in_features,out_features of y = x W + b")
     p.add_argument("--gemm-backend", choices=["tcgen05", "cublas"], default="tcgen05",
                    help="block_stack workload: the bf16 Linear GEMMs on this library's kernel or on cuBLAS")
     p.add_argument("--rope-launches", type=int, choices=[1, 2], default=2,
@@ -637,8 +639,64 @@ def run_block_stack(a):
     return 0
 
 
+def run_linear(a):
+    """One bf16 Linear forward (y = x W + b, W [in, out]) through hx_linear_fwd:
+    the GEMM of the block stack's projections, on the backend --gemm-backend
+    selects (context workload, 1 GPU)."""
+    import ctypes
+
+    import torch
+
+    import haelixe_b200 as hx
+    from haelixe_b200 import _native as N
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    M, K, Nn = (int(x) for x in a.linear_shape.split(","))
+    g = torch.Generator(device=dev).manual_seed(a.seed)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(K, Nn, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
+    b = torch.randn(Nn, device=dev, generator=g).to(torch.bfloat16)
+    y = torch.empty(M, Nn, device=dev, dtype=torch.bfloat16)
+    ctx = hx.context(local)
+    ctx.use_stream()
+    L = N.lib()
+    N.check(L.hx_set_gemm_backend(ctx.handle, 1 if a.gemm_backend == "cublas" else 0), ctx.handle)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+
+    def step():
+        N.check(L.hx_linear_fwd(ctx.handle, N.HX_BF16, p(x), p(w), p(b), p(y), M, K, Nn), ctx.handle)
+
+    for _ in range(a.warmup):
+        step()
+    launches0 = L.hx_kernel_launches(ctx.handle)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(a.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / a.steps
+    tf = 2.0 * M * K * Nn / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": "linear forward TFLOP/s (context workload)", "value": tf, "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": f"linear y = x W + b, rows {M}, in {K}, out {Nn}", "gemm": a.gemm_backend,
+                   "gemm_path": {1: "cublas", 2: "tcgen05"}.get(L.hx_last_gemm_path(ctx.handle), "none")},
+        "gpu_launches": int(L.hx_kernel_launches(ctx.handle) - launches0),
+    }), flush=True)
+    return 0
+
+
 def main():
     a = parse()
+    if a.workload == "linear":
+        return run_linear(a)
     if a.workload == "block_stack":
         return run_block_stack(a)
     if a.impl == "reference":

@@ -336,13 +336,15 @@ cudaError_t gemm_bf16(cudaStream_t st, int sm_count, DeviceStatus* status, bool 
                       const void* R, int64_t ldr, const void* bias, int tile) {
     if (!gemm_bf16_supported(a_mn, b_mn, M, N, K, A, lda, B, ldb, C, ldc, R, ldr, bias))
         return cudaErrorNotSupported;
-    // Tile shape: 256 x 256 reads the least operand data per FLOP (the kernel
-    // is L2-bandwidth bound at small K) but exposes its epilogue once per tile
-    // and fills waves coarsely; 128 x 256 overlaps the epilogue; 128 x 128
-    // serves narrow outputs. `tile` (1, 2, 3) forces one of them.
+    // Tile shape: 256 x 256 reads the least operand data per FLOP but exposes
+    // its epilogue once per tile and fills waves coarsely, so it pays only
+    // when the main loop is long (K >= 4096) and there are enough tiles;
+    // measured on the block stack's shapes, 128 x 256 (epilogue overlapped)
+    // won every K = 2048 product. 128 x 128 serves narrow outputs. `tile`
+    // (1, 2, 3) forces one of them.
     auto tiles_of = [&](int bm, int bn) { return ((M + bm - 1) / bm) * ((N + bn - 1) / bn); };
     int BM = 128, BN = N > 128 ? 256 : 128;
-    if (tile == 0 && N > 128 && M > 128 && tiles_of(256, 256) >= 2 * sm_count &&
+    if (tile == 0 && N > 128 && M > 128 && K >= 4096 && tiles_of(256, 256) * 10 >= 17 * sm_count &&
         wave_fill(tiles_of(256, 256), sm_count) >= 0.85)
         BM = 256;
     if (tile == 1) BM = 128, BN = 128;
