@@ -84,6 +84,9 @@ def parse():
     p.add_argument("--seq", type=int, default=8192)
     p.add_argument("--head-dim", type=int, default=128)
     p.add_argument("--no-causal", action="store_true")
+    p.add_argument("--dtype", choices=["bf16", "f32"], default="bf16",
+                   help="operand dtype of the attention workload; f32 runs on the tensor cores as bf16 "
+                        "hi/lo planes, three MMAs per product")
     p.add_argument("--rope-theta", type=float, default=500000.0)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--e2e-steps", type=int, default=20)
@@ -115,11 +118,11 @@ def attn_flops(B, H, S, D, causal):
 
 def workload_name(a):
     return (f"attention layer core B{a.batch} H{a.heads} S{a.seq} D{a.head_dim} "
-            f"{'causal' if not a.no_causal else 'full'} bf16, RoPE theta {a.rope_theta:g} on Q/K")
+            f"{'causal' if not a.no_causal else 'full'} {a.dtype}, RoPE theta {a.rope_theta:g} on Q/K")
 
 
 def config_of(a, n):
-    op_mb = a.batch * a.heads * a.seq * a.head_dim * 2 / 1e6
+    op_mb = a.batch * a.heads * a.seq * a.head_dim * (4 if a.dtype == "f32" else 2) / 1e6
     return {
         "workload": workload_name(a),
         "batch": a.batch, "heads": a.heads, "seq_len": a.seq, "head_dim": a.head_dim,
@@ -334,17 +337,18 @@ def run_haelixe(a):
     Hl = H // world
     scale = 1.0 / math.sqrt(D)
     ctx = hx.context(local)
+    dt = torch.float32 if a.dtype == "f32" else torch.bfloat16
 
     # Inputs for this rank's heads, generated from the global head index so a
     # head's data does not depend on the GPU count.
     def gen(which):
         if a.head_layout == "bshd":
-            t = torch.empty(B, S, Hl, D, device=dev, dtype=torch.bfloat16).permute(0, 2, 1, 3)
+            t = torch.empty(B, S, Hl, D, device=dev, dtype=dt).permute(0, 2, 1, 3)
         else:
-            t = torch.empty(B, Hl, S, D, device=dev, dtype=torch.bfloat16)
+            t = torch.empty(B, Hl, S, D, device=dev, dtype=dt)
         for hl in range(Hl):
             g = torch.Generator(device=dev).manual_seed(a.seed * 1000003 + which * 1009 + rank * Hl + hl)
-            t[:, hl] = torch.randn(B, S, D, device=dev, generator=g).to(torch.bfloat16)
+            t[:, hl] = torch.randn(B, S, D, device=dev, generator=g).to(dt)
         return t
 
     q, k, v, do = (gen(i) for i in range(4))
@@ -359,10 +363,10 @@ def run_haelixe(a):
     if world > 1:
         # The forward writes O straight into this rank's slot of the group's
         # gather buffer, so the all-gather runs in place.
-        gbuf = group.gather_buffer((B, Hl, S, D), torch.bfloat16)
+        gbuf = group.gather_buffer((B, Hl, S, D), dt)
         bufs0["o"] = (gbuf[rank].view(B, S, Hl, D).permute(0, 2, 1, 3) if a.head_layout == "bshd"
                       else gbuf[rank])
-        merged = torch.empty(B, S, H, D, device=dev, dtype=torch.bfloat16)
+        merged = torch.empty(B, S, H, D, device=dev, dtype=dt)
     qr, kr, o, lse = bufs0["qr"], bufs0["kr"], bufs0["o"], bufs0["lse"]
     dv, dq0, dk0 = bufs0["dv"], bufs0["dq0"], bufs0["dk0"]
     stream = torch.cuda.current_stream(dev)
@@ -459,16 +463,20 @@ def run_haelixe(a):
     dom_flops = (10.0 if dom == "bwd" else 4.0) * B * Hl * S * S * D * (0.5 if causal else 1.0)
     dom_ms = bwd_ms if dom == "bwd" else fwd_ms
     achieved = dom_flops / (dom_ms * 1e-3) / 1e12
+    # f32 runs three bf16 MMAs per product: the tensor pipe does 3x the
+    # attention FLOPs, and that issued work is what the bf16 peak bounds.
+    split = 3.0 if a.dtype == "f32" else 1.0
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+            "vs_baseline": None, "dtype": a.dtype, "data": "synthetic (seeded N(0,1))",
             "config": config_of(a, world),
             "roofline": {"bound": "tensor", "kernel": f"attention {dom} ({ctx.last_path})",
                          "achieved": achieved, "peak": peak, "peak_source": peak_src,
-                         "unit": "TFLOP/s", "frac": achieved / peak,
-                         "traffic": traffic_per_launch(dom, B, Hl, S, D)},
+                         "unit": "TFLOP/s", "frac": achieved * split / peak,
+                         "mma_flops_per_flop": split,
+                         "traffic": traffic_per_launch(dom, B, Hl, S, D) if split == 1.0 else None},
             "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
             "fraction_of_peak": value / world / peak,
             "gpu_launches": int(launches),

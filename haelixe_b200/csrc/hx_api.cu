@@ -426,16 +426,26 @@ int hx_attn_fwd_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, cons
     const hx::AttnDims d = hx::dims_of(*shape);
     const bool fast = !c->force_simt && lse != nullptr && hx::sm100_supported(dt, d) &&
                       tma_layout_ok(d, {q, k, v, o});
+    // f32 at head_dim 64/128: tcgen05 on bf16 hi/lo operand planes (a
+    // workspace from the context's arena, released stream-ordered).
+    const bool split = !c->force_simt && lse != nullptr && !fast && hx::split_supported(dt, d);
     cudaError_t e;
     if (fast) {
         e = hx::sm100_attn_fwd(c->stream, c->sm_count, c->status, d, q, k, v, o, lse, scale,
                                causal);
         c->last_path = 2;
+    } else if (split) {
+        void* ws = nullptr;
+        if ((st = hx_alloc(c, hx::split_fwd_workspace_bytes(d), &ws))) return st;
+        e = hx::split_attn_fwd(c->stream, c->sm_count, c->status, d, q, k, v, o, lse, scale, causal, ws);
+        hx_free(c, ws);
+        c->last_path = 2;
     } else {
         e = hx::simt_attn_fwd(c->stream, dt, d, q, k, v, o, lse, scale, causal);
         c->last_path = 1;
     }
-    return check_cuda(c, e, fast ? "attention forward (tcgen05)" : "attention forward (SIMT)");
+    return check_cuda(c, e, fast ? "attention forward (tcgen05)"
+                                 : split ? "attention forward (tcgen05, split f32)" : "attention forward (SIMT)");
 }
 
 int hx_attn_bwd_workspace_size(hx_dtype dt, const hx_attn_shape* shape, uint64_t* bytes) {
@@ -448,6 +458,7 @@ int hx_attn_bwd_workspace_size(hx_dtype dt, const hx_attn_shape* shape, uint64_t
     const hx::AttnDims d = hx::dims_of(*shape);
     uint64_t n = simt_ws_bytes(d);
     if (hx::sm100_bwd_supported(dt, d)) n = std::max(n, hx::sm100_bwd_workspace_bytes(d));
+    if (hx::split_supported(dt, d)) n = std::max(n, hx::split_bwd_workspace_bytes(d));
     *bytes = n;
     return HX_OK;
 }
@@ -501,7 +512,10 @@ static int attn_bwd_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, c
     const hx::AttnDims d = hx::dims_of(*shape);
     const bool fast = !c->force_simt && hx::sm100_bwd_supported(dt, d) &&
                       tma_layout_ok(d, {q, k, v, o, dout, dq, dk, dv});
-    const uint64_t need = fast ? hx::sm100_bwd_workspace_bytes(d) : simt_ws_bytes(d);
+    const bool split = !c->force_simt && !fast && hx::split_supported(dt, d);
+    const uint64_t need = fast    ? hx::sm100_bwd_workspace_bytes(d)
+                          : split ? hx::split_bwd_workspace_bytes(d)
+                                  : simt_ws_bytes(d);
     void* ws = workspace;
     bool owned = false;
     if (ws == nullptr) {
@@ -520,6 +534,14 @@ static int attn_bwd_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, c
         e = hx::sm100_attn_bwd(c->stream, c->sm_count, c->status, d, q, k, v, o, dout, lse, dq, dk,
                                dv, ws, scale, causal, tab);
         c->last_path = 2;
+    } else if (split) {
+        e = hx::split_attn_bwd(c->stream, c->sm_count, c->status, d, q, k, v, o, dout, lse, dq, dk, dv, ws, scale,
+                               causal);
+        if (e == cudaSuccess && tab != nullptr) {  // dQ and dK rotated back in place after the kernel
+            e = hx::rope_apply(c->stream, c->sm_count, dt, d, dq, dq, tab, -1.f);
+            if (e == cudaSuccess) e = hx::rope_apply(c->stream, c->sm_count, dt, d, dk, dk, tab, -1.f);
+        }
+        c->last_path = 2;
     } else {
         e = hx::simt_attn_bwd(c->stream, dt, d, q, k, v, o, dout, lse, dq, dk, dv, (float*)ws,
                               scale, causal);
@@ -529,7 +551,9 @@ static int attn_bwd_common(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, c
         }
         c->last_path = 1;
     }
-    st = check_cuda(c, e, fast ? "attention backward (tcgen05)" : "attention backward (SIMT)");
+    st = check_cuda(c, e, fast    ? "attention backward (tcgen05)"
+                          : split ? "attention backward (tcgen05, split f32)"
+                                  : "attention backward (SIMT)");
     if (owned) hx_free(c, ws);  // stream-ordered: the next user of the slab queues behind us
     return st;
 }

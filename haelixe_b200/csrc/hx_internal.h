@@ -99,6 +99,18 @@ cudaError_t sm100_attn_bwd(cudaStream_t st, int sm_count, DeviceStatus* status,
                            void* dk, void* dv, void* workspace, float scale, int causal,
                            const float2* rope_tab = nullptr);
 
+// ---- tcgen05 kernels for f32 I/O by operand splitting (attn_split_sm100.cu): D in {64,128} ----
+// Each f32 operand as bf16 hi + lo planes, every product as three bf16 UMMAs.
+bool split_supported(hx_dtype dt, const AttnDims& d);
+uint64_t split_fwd_workspace_bytes(const AttnDims& d);
+uint64_t split_bwd_workspace_bytes(const AttnDims& d);
+cudaError_t split_attn_fwd(cudaStream_t st, int sm_count, DeviceStatus* status, const AttnDims& d, const void* q,
+                           const void* k, const void* v, void* o, float* lse, float scale, int causal, void* ws);
+// dq/dk/dv are f32; dq is zeroed and accumulated in place (red.global.add).
+cudaError_t split_attn_bwd(cudaStream_t st, int sm_count, DeviceStatus* status, const AttnDims& d, const void* q,
+                           const void* k, const void* v, const void* o, const void* dout, const float* lse,
+                           void* dq, void* dk, void* dv, void* ws, float scale, int causal);
+
 // ---- the attention block around the kernel (mha_ops.cu) ----
 cudaError_t rmsnorm_fwd(cudaStream_t st, int sm_count, hx_dtype dt, const void* x, const void* w, void* y,
                         int rows, int hidden, float eps);
