@@ -4,24 +4,33 @@
 // arithmetic the reference does in f32 (src/gpu/shaders/flash_attention.wgsl:
 // 19-123, src/tensor.rs:395-397), for head_dim 64 and 128.
 //
-// Every f32 operand x travels as two bf16 planes, hi = bf16(x) and
-// lo = bf16(x - hi): |x - hi| <= 2^-8 |x| (half a bf16 ulp), so hi + lo =
-// x (1 + e) with |e| <= 2^-16. A product A.B is three bf16 UMMAs into one f32
-// TMEM accumulator,
+// Every f32 operand x travels as two fp16 planes of y = x * 2^e, hi = f16(y)
+// and lo = f16(y - hi), where the power of two 2^e brings the operand's
+// largest magnitude into [2^14, 2^15): |y - hi| <= 2^-11 |y| and lo keeps 11
+// more bits, so hi + lo = y (1 + r) with |r| <= 2^-22 (elements below 2^-17
+// of the largest keep an absolute error under 2^-39 of it). A product A.B is
+// three f16 UMMAs into one f32 TMEM accumulator,
 //     A_hi.B_lo + A_lo.B_hi + A_hi.B_hi,
-// the dropped A_lo.B_lo being at most 2^-16 |A||B| per term: at most 3 * 2^-16
-// (5e-5) relative per elementary product and about 1e-5 in practice, against
-// f32's 6e-8 and the 1e-3 absolute bound the f32 path is held to. bf16 pairs
-// rather than TF32 pairs keep the f16-kind MMA rate (twice kind::tf32) and two
-// bytes per plane element, which is what lets Q, K and V of both planes stay
-// on chip at head_dim 128.
+// the dropped A_lo.B_lo being at most 2^-22 |A||B| per term, and the scales
+// come off exactly (powers of two) where the accumulators are read. That is
+// the precision of a 3xTF32 split at the f16-kind MMA rate (twice kind::tf32)
+// and two bytes per plane element, which is what lets Q, K and V of both
+// planes stay on chip at head_dim 128. (bf16 planes would carry only 16 bits:
+// 2^-16 per operand, too coarse for the 1e-3 bound on weight gradients of
+// magnitude ~100 that the f32 layer's tests hold.)
 //
-//   split_pre   f32 Q, K, V (and dO) -> contiguous bf16 hi/lo planes
+// Scales: Q, K, V, dO per tensor from their max-abs (split_stats); P by 2^14
+// in the backward (P <= 1) and 2^6 in the forward (P <= 2^8 under lazy
+// rescaling); dS by the bound |dS| <= |dP| + |delta| <= 2 max|dO_q|
+// max|V_k| (row 2-norms; O is a convex combination of V rows).
+//
+//   split_stats max-abs and largest row 2-norm of each f32 operand.
+//   split_pre   f32 Q, K, V (and dO) -> contiguous f16 hi/lo planes
 //               [B*H][S][D]; in the backward also lse * log2(e),
 //               delta = rowsum(dO * O) in f32, and dQ := 0.
 //   fwd         two 128-row query tiles per CTA, K/V rings of BN-key tiles:
 //               S = Q K^T (SS), P = exp2(S*scale*log2e - m) written back over
-//               S as packed hi | lo bf16, O += P V (TS, P from TMEM); online
+//               S as packed hi | lo f16, O += P V (TS, P from TMEM); online
 //               softmax with lazy rescaling and ping-pong warpgroups.
 //   bwd         one CTA per 128-key tile, K and V resident, looping over query
 //               tiles of BQ rows: S^T = K Q^T, dP^T = V dO^T, P^T and
@@ -34,6 +43,8 @@
 // copies and MMAs, frees its TMEM and exits; hx_sync reports HX_ERR_TIMEOUT.
 #include <math.h>
 #include <string.h>
+
+#include <cuda_fp16.h>
 
 #include <initializer_list>
 
@@ -50,18 +61,68 @@ constexpr float kLn2 = 0.6931471805599453f;
 
 __device__ __forceinline__ uint32_t bar_addr(const uint64_t& b) { return smem_addr(&b); }
 
-// (a, b) -> packed bf16 hi = (bf16(a), bf16(b)) and lo = (bf16(a - hi_a),
-// bf16(b - hi_b)); the low halves hold a.
-__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
-    hi = pack_bf16(a, b);
-    const float ah = __uint_as_float(hi << 16), bh = __uint_as_float(hi & 0xffff0000u);
-    lo = pack_bf16(a - ah, b - bh);
+// Packed f16 pair, round to nearest even; the low half holds `lo`.
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ float f16_lo(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xffffu))); }
+__device__ __forceinline__ float f16_hi(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v >> 16))); }
+
+// (a, b) scaled by the power of two s -> packed f16 hi = (f16(a s), f16(b s))
+// and lo = (f16(a s - hi_a), f16(b s - hi_b)); the low halves hold a. The
+// differences a s - hi_a are exact in f32.
+__device__ __forceinline__ void split2(float a, float b, float s, uint32_t& hi, uint32_t& lo) {
+    const float ya = a * s, yb = b * s;
+    hi = pack_f16(ya, yb);
+    lo = pack_f16(ya - f16_lo(hi), yb - f16_hi(hi));
 }
 
-// One f32 operand as its two bf16 planes, each contiguous [B*H][S][D].
+// Power of two that brings a non-negative magnitude m (as f32 bits) into
+// [2^14, 2^15): 2^(14 - floor(log2 m)); 1 for 0, inf or NaN, and clamped to
+// stay a normal f32.
+__host__ __device__ __forceinline__ float pow2_scale(uint32_t bits) {
+    const int ex = (int)((bits >> 23) & 0xffu);
+    if (bits == 0u || ex == 0xff) return 1.f;
+    int e = 14 - (ex - 127);
+    e = e < -120 ? -120 : (e > 120 ? 120 : e);
+    union {
+        uint32_t u;
+        float f;
+    } r;
+    r.u = (uint32_t)(e + 127) << 23;
+    return r.f;
+}
+// P planes: the backward's P = exp2(s - lse) is at most 1 and goes in scaled
+// by 2^14; the forward's P is relative to a running max that may lag the true
+// one by up to 2^kRescaleLog2 = 2^8 (lazy rescaling), so it goes in by 2^6.
+constexpr float kPScaleBwd = 16384.f;
+constexpr float kPScaleFwd = 64.f;
+
+// Instruction descriptor of a kind::f16 UMMA with f16 A and B (format 0) and
+// f32 accumulation: the bf16 descriptor with both operand formats cleared.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn_major, bool b_mn_major) {
+    return idesc_bf16_f32(M, N, a_mn_major, b_mn_major) & ~((1u << 7) | (1u << 10));
+}
+
+// Operand statistics (device, zeroed before split_stats): f32 bits of the
+// max-abs and of the largest row 2-norm squared of q, k, v, dout.
+struct Stats {
+    uint32_t maxabs[4];
+    uint32_t maxn2[4];
+};
+
+// Scale of the dS planes from the bound |dS| <= 2 max|dO_q| max|V_k|.
+__device__ __forceinline__ float ds_scale(const Stats* st) {
+    const float b = 2.f * sqrtf(__uint_as_float(st->maxn2[3])) * sqrtf(__uint_as_float(st->maxn2[2]));
+    return pow2_scale(__float_as_uint(b));
+}
+
+// One f32 operand as its two f16 planes, each contiguous [B*H][S][D].
 struct Planes {
-    __nv_bfloat16* hi;
-    __nv_bfloat16* lo;
+    __half* hi;
+    __half* lo;
 };
 
 struct PreParams {
@@ -73,6 +134,7 @@ struct PreParams {
     float* lse2;          // backward: [B*H][S_pad] lse * log2(e), 0 past S
     float* delta;         // backward: [B*H][S_pad] rowsum(dO * O), 0 past S
     float* dq;            // backward: zeroed, strided like the operands
+    Stats* stats;         // written by split_stats, read by split_pre
     int S_pad;
 };
 
@@ -80,6 +142,57 @@ template <bool VEC>
 __device__ __forceinline__ float4 load4(const float* p) {
     if (VEC) return *reinterpret_cast<const float4*>(p);
     return make_float4(p[0], p[1], p[2], p[3]);
+}
+
+// Max-abs and largest row 2-norm squared of each operand: D/4 lanes per row
+// (one float4 each), grid-stride over the rows [B*H][S]; per-thread running
+// maxima, one atomicMax per warp and operand at the end (non-negative f32
+// values order like their bits).
+template <int D, bool VEC>
+__global__ void __launch_bounds__(256) split_stats_kernel(const PreParams p, const AttnDims d) {
+    constexpr int G = D / 4;
+    constexpr int RPW = 32 / G;
+    const int64_t rows = (int64_t)d.B * d.H * d.S;
+    const int lane = threadIdx.x % 32, sub = lane % G;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x / 32);
+    float mabs[4] = {0.f, 0.f, 0.f, 0.f}, mn2[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int64_t r0 = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * RPW; r0 < rows;
+         r0 += nwarps * RPW) {
+        const int64_t r = r0 + lane / G;
+        const bool row_ok = r < rows;
+        const int64_t bhi = row_ok ? r / d.S : 0;
+        const int s = row_ok ? (int)(r % d.S) : 0;
+        const int64_t off = (bhi / d.H) * d.sb + (bhi % d.H) * d.sh + (int64_t)s * d.ss + sub * 4;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            if (t < p.n) {
+                float n2 = 0.f;
+                if (row_ok) {
+                    const float4 x = load4<VEC>(p.src[t] + off);
+                    mabs[t] = fmaxf(mabs[t], fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+                    n2 = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+                }
+#pragma unroll
+                for (int w = G / 2; w > 0; w >>= 1) n2 += __shfl_xor_sync(0xffffffffu, n2, w);
+                mn2[t] = fmaxf(mn2[t], n2);
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        if (t < p.n) {
+            float a = mabs[t], n2 = mn2[t];
+#pragma unroll
+            for (int w = 16; w > 0; w >>= 1) {
+                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, w));
+                n2 = fmaxf(n2, __shfl_xor_sync(0xffffffffu, n2, w));
+            }
+            if (lane == 0) {
+                atomicMax(&p.stats->maxabs[t], __float_as_uint(a));
+                atomicMax(&p.stats->maxn2[t], __float_as_uint(n2));
+            }
+        }
+    }
 }
 
 // D/4 lanes per row (one float4 each), 32/(D/4) rows per warp, grid-stride
@@ -92,6 +205,9 @@ __global__ void __launch_bounds__(256) split_pre_kernel(const PreParams p, const
     const int lane = threadIdx.x % 32, sub = lane % G;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x / 32);
     const bool bwd = p.o != nullptr;
+    float sc[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) sc[t] = pow2_scale(p.stats->maxabs[t]);
     for (int64_t r0 = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * RPW; r0 < rows;
          r0 += nwarps * RPW) {
         const int64_t r = r0 + lane / G;
@@ -109,8 +225,8 @@ __global__ void __launch_bounds__(256) split_pre_kernel(const PreParams p, const
                 if (t < p.n) {
                     const float4 x = load4<VEC>(p.src[t] + off);
                     uint2 hi, lo;
-                    split2(x.x, x.y, hi.x, lo.x);
-                    split2(x.z, x.w, hi.y, lo.y);
+                    split2(x.x, x.y, sc[t], hi.x, lo.x);
+                    split2(x.z, x.w, sc[t], hi.y, lo.y);
                     *reinterpret_cast<uint2*>(p.dst[t].hi + poff) = hi;
                     *reinterpret_cast<uint2*>(p.dst[t].lo + poff) = lo;
                 }
@@ -198,6 +314,7 @@ struct Params {
     int causal;
     int hgroup;  // (batch, head) slices per dispatch group
     int vec;     // o rows 16-byte aligned: float4 stores
+    const Stats* stats;  // plane scales of q, k, v
     DeviceStatus* status;
 };
 
@@ -324,8 +441,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp < 4) {
         // ------------------------------------------------------------ MMA issuer (warp 1, lane 0)
         if (warp == 1 && lane == 0) {
-            constexpr uint32_t idS = idesc_bf16_f32(BM, BN, false, false);
-            constexpr uint32_t idO = idesc_bf16_f32(BM, D, false, true);
+            constexpr uint32_t idS = idesc_f16(BM, BN, false, false);
+            constexpr uint32_t idO = idesc_f16(BM, D, false, true);
             // Every descriptor shares the high word (SBO 1024, 128-byte swizzle);
             // a plane, stage, tile or K step only moves the start address in the
             // low word, so each is a 32-bit add to a base built once.
@@ -425,6 +542,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tS = tl + (w ? C::S_COL1 : C::S_COL0);
         const uint32_t tO = tl + (w ? C::O_COL1 : C::O_COL0);
         const int nt = n_w[w];
+        // S leaves the MMA scaled by sq * sk and O by kPScaleFwd * sv (powers of two).
+        const float sq = pow2_scale(p.stats->maxabs[0]), sk = pow2_scale(p.stats->maxabs[1]),
+                    sv = pow2_scale(p.stats->maxabs[2]);
+        const float sl2 = p.sl2 / (sq * sk);
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
         for (int j = 0; j < nt; ++j) {
@@ -460,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     !(ok = mbar_wait(bar_addr(bars->turn[w]), jt & 1, abort_flag, p.status, 133)))
                     break;
             }
-            const float m_new = fmaxf(m_run, mx * p.sl2);
+            const float m_new = fmaxf(m_run, mx * sl2);
             float m_use = m_run, alpha = 1.f;
             bool rescale = false;
             if (j == 0) {
@@ -485,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_st32(tO + c, o);
                 }
             }
-            const uint64_t sl2x2 = f2_pack(p.sl2, p.sl2);
+            const uint64_t sl2x2 = f2_pack(sl2, sl2);
             const uint64_t negx2 = f2_pack(-m_use, -m_use);
             uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = sum_a;
             // P as hi | lo planes over the S columns: hi packed into columns
@@ -504,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         sum_b = f2_add(sum_b, f2_pack(p0, p1));
                     else
                         sum_a = f2_add(sum_a, f2_pack(p0, p1));
-                    split2(p0, p1, ph[i], pl[i]);
+                    split2(p0, p1, kPScaleFwd, ph[i], pl[i]);
                 }
                 tmem_st16(tS + c / 2, ph);
                 tmem_st16(tS + BN / 2 + c / 2, pl);
@@ -525,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ok && nt > 0 && mbar_wait(bar_addr(bars->o_full[w]), (nt - 1) & 1, abort_flag, p.status, 132)) {
             tc_fence_after();
-            const float inv = 1.f / l_run;
+            const float inv = 1.f / (l_run * kPScaleFwd * sv);
             const bool store = row < p.S;
             float* orow = p.o + (int64_t)b * p.sb + (int64_t)h * p.sh + (int64_t)row * p.ss;
 #pragma unroll
@@ -626,6 +747,7 @@ struct Params {
     int causal;
     int hgroup;  // (batch, head) slices per dispatch group
     int vec;     // dk/dv rows 16-byte aligned: float4 stores
+    const Stats* stats;  // plane scales of q, k, v, dout and the dS bound
     DeviceStatus* status;
 };
 
@@ -744,9 +866,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // dP^T runs), dV once P^T is in TMEM, dK once dS^T is, then dQ. Each
         // product is hi.lo + lo.hi + hi.hi over the two planes.
         if (warp == 1 && lane == 0) {
-            constexpr uint32_t idSP = idesc_bf16_f32(BK, BQ, false, false);
-            constexpr uint32_t idAcc = idesc_bf16_f32(BK, D, false, true);
-            constexpr uint32_t idDQ = C::DQ_T ? idesc_bf16_f32(D, BQ, true, true) : idesc_bf16_f32(BQ, D, true, true);
+            constexpr uint32_t idSP = idesc_f16(BK, BQ, false, false);
+            constexpr uint32_t idAcc = idesc_f16(BK, D, false, true);
+            constexpr uint32_t idDQ = C::DQ_T ? idesc_f16(D, BQ, true, true) : idesc_f16(BQ, D, true, true);
             constexpr int NS = D / 16;   // K steps of S^T, dP^T
             constexpr int NA = BQ / 16;  // K steps of dV, dK
             constexpr int NQ = BK / 16;  // K steps of dQ
@@ -838,7 +960,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = wi * 32 + lane;
         const int kr = k0 + r;
         const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
-        const float sl2 = p.scale * kLog2e;
+        // S^T leaves the MMA scaled by sk * sq, dP^T by sv * sdo; P^T and dS^T
+        // go in scaled by kPScaleBwd and sds (powers of two: exact).
+        const float sq = pow2_scale(p.stats->maxabs[0]), sk = pow2_scale(p.stats->maxabs[1]),
+                    sv = pow2_scale(p.stats->maxabs[2]), sdo = pow2_scale(p.stats->maxabs[3]);
+        const float sds = ds_scale(p.stats);
+        const float sl2 = p.scale * kLog2e / (sk * sq);
+        const float dpu = 1.f / (sv * sdo);
         const int c0 = g * HC;
         bool ok = true;
         for (int it = 0; it < n_it; ++it) {
@@ -878,7 +1006,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < HC; c += 32) {
                 uint32_t ph[16], pl[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) split2(pr[c + 2 * i], pr[c + 2 * i + 1], ph[i], pl[i]);
+                for (int i = 0; i < 16; ++i) split2(pr[c + 2 * i], pr[c + 2 * i + 1], kPScaleBwd, ph[i], pl[i]);
                 tmem_st16(tl + C::C_S + c0 + c / 2, ph);
                 tmem_st16(tl + C::C_S + c0 + HC / 2 + c / 2, pl);
             }
@@ -896,10 +1024,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int q4 = 0; q4 < HC / 4; ++q4) {
                 const float4 d4 = reinterpret_cast<const float4*>(del)[q4];
-                pr[4 * q4 + 0] *= __uint_as_float(x[4 * q4 + 0]) - d4.x;
-                pr[4 * q4 + 1] *= __uint_as_float(x[4 * q4 + 1]) - d4.y;
-                pr[4 * q4 + 2] *= __uint_as_float(x[4 * q4 + 2]) - d4.z;
-                pr[4 * q4 + 3] *= __uint_as_float(x[4 * q4 + 3]) - d4.w;
+                pr[4 * q4 + 0] *= fmaf(__uint_as_float(x[4 * q4 + 0]), dpu, -d4.x);
+                pr[4 * q4 + 1] *= fmaf(__uint_as_float(x[4 * q4 + 1]), dpu, -d4.y);
+                pr[4 * q4 + 2] *= fmaf(__uint_as_float(x[4 * q4 + 2]), dpu, -d4.z);
+                pr[4 * q4 + 3] *= fmaf(__uint_as_float(x[4 * q4 + 3]), dpu, -d4.w);
             }
             // The smem dS tile is free once dQ(it - 1) has read it.
             if (!(ok = mbar_wait(bar_addr(bars->dsfree), (it & 1) ^ 1, abort_flag, p.status, 164))) break;
@@ -907,7 +1035,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < HC; c += 32) {
                 uint32_t dh[16], dl[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) split2(pr[c + 2 * i], pr[c + 2 * i + 1], dh[i], dl[i]);
+                for (int i = 0; i < 16; ++i) split2(pr[c + 2 * i], pr[c + 2 * i + 1], sds, dh[i], dl[i]);
                 // dS^T hi | lo in TMEM over the dP^T columns (A of dK) ...
                 tmem_st16(tl + C::C_DP + c0 + c / 2, dh);
                 tmem_st16(tl + C::C_DP + c0 + HC / 2 + c / 2, dl);
@@ -934,7 +1062,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const bool store = kr < p.S;
             const uint32_t col = g ? C::C_DK : C::C_DV;
-            const float mul = g ? p.scale : 1.f;
+            const float mul = g ? p.scale / (sds * sq) : 1.f / (kPScaleBwd * sdo);
             float* dst = (g ? p.dk : p.dv) + (int64_t)b * p.sb + (int64_t)h * p.sh + (int64_t)kr * p.ss;
 #pragma unroll
             for (int c = 0; c < D; c += 32) {
@@ -969,6 +1097,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = wi * 32 + lane;
         const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
         float* base = p.dq + (int64_t)b * p.sb + (int64_t)h * p.sh;
+        const float mul = p.scale / (ds_scale(p.stats) * pow2_scale(p.stats->maxabs[1]));  // dQ = scale dS K
         for (int it = 0; it < n_it; ++it) {
             const int q0 = (i_start + it) * BQ;
             if (!mbar_wait(bar_addr(bars->dq_full), it & 1, abort_flag, p.status, 170)) break;
@@ -985,12 +1114,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float* dst = base + (int64_t)q0 * p.ss + r;
 #pragma unroll
                 for (int c = 0; c < BQ; ++c)
-                    if (c < nq) red_add_f32(dst + (int64_t)c * p.ss, __uint_as_float(v[c]) * p.scale);
+                    if (c < nq) red_add_f32(dst + (int64_t)c * p.ss, __uint_as_float(v[c]) * mul);
             } else {
                 if (q0 + r < p.S) {
                     float* dst = base + (int64_t)(q0 + r) * p.ss;
 #pragma unroll
-                    for (int c = 0; c < D; ++c) red_add_f32(dst + c, __uint_as_float(v[c]) * p.scale);
+                    for (int c = 0; c < D; ++c) red_add_f32(dst + c, __uint_as_float(v[c]) * mul);
                 }
             }
         }
@@ -1010,16 +1139,21 @@ int s_pad_of(const AttnDims& d) { return (d.S + 127) / 128 * 128; }
 
 uint64_t table_bytes(const AttnDims& d) { return align256((uint64_t)d.B * d.H * s_pad_of(d) * 4); }
 
-// Workspace: n operands x (hi, lo) planes, 256-byte aligned each.
-void carve_planes(void* ws, const AttnDims& d, int n, Planes* out) {
-    uint8_t* p = (uint8_t*)ws;
+// Workspace: the Stats block (256 bytes), then n operands x (hi, lo) planes,
+// 256-byte aligned each.
+constexpr uint64_t kStatsBytes = 256;
+static_assert(sizeof(Stats) <= kStatsBytes, "stats block");
+
+Stats* carve_planes(void* ws, const AttnDims& d, int n, Planes* out) {
+    uint8_t* p = (uint8_t*)ws + kStatsBytes;
     const uint64_t pb = plane_bytes(d);
     for (int i = 0; i < n; ++i) {
-        out[i].hi = (__nv_bfloat16*)p;
+        out[i].hi = (__half*)p;
         p += pb;
-        out[i].lo = (__nv_bfloat16*)p;
+        out[i].lo = (__half*)p;
         p += pb;
     }
+    return (Stats*)ws;
 }
 
 // float4 access to every operand row: 16-byte aligned bases, strides in
@@ -1031,22 +1165,35 @@ bool vec_ok(const AttnDims& d, std::initializer_list<const void*> ptrs) {
     return true;
 }
 
-// A plane [B][H][S][D] (contiguous) as a TMA map with box (64, rows).
-bool plane_map(CUtensorMap* m, const __nv_bfloat16* base, const AttnDims& d, int rows) {
+// A plane [B][H][S][D] (contiguous f16) as a TMA map with box (64, rows).
+bool plane_map(CUtensorMap* m, const __half* base, const AttnDims& d, int rows) {
     return make_tmap_bhsd(m, base, d.B, d.H, d.S, d.D, (int64_t)d.H * d.S * d.D, (int64_t)d.S * d.D, d.D, 64,
-                          rows);
+                          rows, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
 }
 
-template <int D>
-cudaError_t launch_pre(cudaStream_t st, int sm_count, const PreParams& pp, const AttnDims& d, bool vec) {
-    const int64_t rows = (int64_t)d.B * d.H * pp.S_pad;
+int64_t pre_blocks(int64_t rows, int D, int sm_count) {
     int64_t blocks = (rows / (32 / (D / 4)) + 7) / 8;  // 8 warps per block
     if (blocks > (int64_t)sm_count * 16) blocks = (int64_t)sm_count * 16;
-    if (blocks < 1) blocks = 1;
+    return blocks < 1 ? 1 : blocks;
+}
+
+// Zeroes the Stats block, gathers the operand statistics, then writes the planes.
+template <int D>
+cudaError_t launch_pre(cudaStream_t st, int sm_count, const PreParams& pp, const AttnDims& d, bool vec) {
+    cudaError_t e = cudaMemsetAsync(pp.stats, 0, sizeof(Stats), st);
+    if (e != cudaSuccess) return e;
+    const int64_t sb = pre_blocks((int64_t)d.B * d.H * d.S, D, sm_count);
     if (vec)
-        split_pre_kernel<D, true><<<(unsigned)blocks, 256, 0, st>>>(pp, d);
+        split_stats_kernel<D, true><<<(unsigned)sb, 256, 0, st>>>(pp, d);
     else
-        split_pre_kernel<D, false><<<(unsigned)blocks, 256, 0, st>>>(pp, d);
+        split_stats_kernel<D, false><<<(unsigned)sb, 256, 0, st>>>(pp, d);
+    note_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const int64_t pb = pre_blocks((int64_t)d.B * d.H * pp.S_pad, D, sm_count);
+    if (vec)
+        split_pre_kernel<D, true><<<(unsigned)pb, 256, 0, st>>>(pp, d);
+    else
+        split_pre_kernel<D, false><<<(unsigned)pb, 256, 0, st>>>(pp, d);
     note_launch();
     return cudaGetLastError();
 }
@@ -1068,9 +1215,10 @@ cudaError_t launch_fwd(cudaStream_t st, int sm_count, DeviceStatus* status, cons
                        const float* k, const float* v, float* o, float* lse, float scale, int causal, void* ws) {
     using C = fwd::Cfg<D>;
     Planes pl[3];
-    carve_planes(ws, d, 3, pl);
+    Stats* stats = carve_planes(ws, d, 3, pl);
     PreParams pp;
     memset(&pp, 0, sizeof pp);
+    pp.stats = stats;
     pp.src[0] = q;
     pp.src[1] = k;
     pp.src[2] = v;
@@ -1101,6 +1249,7 @@ cudaError_t launch_fwd(cudaStream_t st, int sm_count, DeviceStatus* status, cons
     prm.causal = causal;
     prm.hgroup = 8;
     prm.vec = vec ? 1 : 0;
+    prm.stats = stats;
     prm.status = status;
     const int64_t blocks = (int64_t)((d.S + fwd::NWG * fwd::BM - 1) / (fwd::NWG * fwd::BM)) * d.H * d.B;
     if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
@@ -1116,10 +1265,11 @@ cudaError_t launch_bwd(cudaStream_t st, int sm_count, DeviceStatus* status, cons
                        float* dq, float* dk, float* dv, void* ws, float scale, int causal) {
     using C = bwd::Cfg<D>;
     Planes pl[4];
-    carve_planes(ws, d, 4, pl);
-    uint8_t* tail = (uint8_t*)ws + 8 * plane_bytes(d);
+    Stats* stats = carve_planes(ws, d, 4, pl);
+    uint8_t* tail = (uint8_t*)ws + kStatsBytes + 8 * plane_bytes(d);
     PreParams pp;
     memset(&pp, 0, sizeof pp);
+    pp.stats = stats;
     pp.src[0] = q;
     pp.src[1] = k;
     pp.src[2] = v;
@@ -1161,6 +1311,7 @@ cudaError_t launch_bwd(cudaStream_t st, int sm_count, DeviceStatus* status, cons
     prm.causal = causal;
     prm.hgroup = 2;
     prm.vec = vec ? 1 : 0;
+    prm.stats = stats;
     prm.status = status;
     const int64_t blocks = (int64_t)((d.S + bwd::BK - 1) / bwd::BK) * d.H * d.B;
     if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
@@ -1174,9 +1325,11 @@ cudaError_t launch_bwd(cudaStream_t st, int sm_count, DeviceStatus* status, cons
 
 bool split_supported(hx_dtype dt, const AttnDims& d) { return dt == HX_F32 && (d.D == 64 || d.D == 128); }
 
-uint64_t split_fwd_workspace_bytes(const AttnDims& d) { return 6 * plane_bytes(d); }
+uint64_t split_fwd_workspace_bytes(const AttnDims& d) { return kStatsBytes + 6 * plane_bytes(d); }
 
-uint64_t split_bwd_workspace_bytes(const AttnDims& d) { return 8 * plane_bytes(d) + 2 * table_bytes(d); }
+uint64_t split_bwd_workspace_bytes(const AttnDims& d) {
+    return kStatsBytes + 8 * plane_bytes(d) + 2 * table_bytes(d);
+}
 
 cudaError_t split_attn_fwd(cudaStream_t st, int sm_count, DeviceStatus* status, const AttnDims& d, const void* q,
                            const void* k, const void* v, void* o, float* lse, float scale, int causal, void* ws) {

@@ -26,10 +26,12 @@ inline EncodeTiledFn encode_tiled_fn() {
     return fn;
 }
 
-// bf16 tensor viewed as [B, H, S, D] (D contiguous; strides in elements),
-// box = (box_d, box_rows, 1, 1), 128-byte swizzle; rows beyond S read as 0.
+// 16-bit (bf16, or f16 with `type`) tensor viewed as [B, H, S, D] (D
+// contiguous; strides in elements), box = (box_d, box_rows, 1, 1), 128-byte
+// swizzle; rows beyond S read as 0.
 inline bool make_tmap_bhsd(CUtensorMap* map, const void* base, int B, int H, int S, int D,
-                           int64_t sb, int64_t sh, int64_t ss, int box_d, int box_rows) {
+                           int64_t sb, int64_t sh, int64_t ss, int box_d, int box_rows,
+                           CUtensorMapDataType type = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
     EncodeTiledFn fn = encode_tiled_fn();
     if (fn == nullptr) return false;
     // A dimension of extent 1 never advances, so any legal stride will do.
@@ -41,7 +43,7 @@ inline bool make_tmap_bhsd(CUtensorMap* map, const void* base, int B, int H, int
                              (cuuint64_t)batch_bytes};
     cuuint32_t box[4] = {(cuuint32_t)box_d, (cuuint32_t)box_rows, 1, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+    CUresult r = fn(map, type, 4, const_cast<void*>(base), dims,
                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

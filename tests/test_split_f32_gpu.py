@@ -1,14 +1,15 @@
 """f32 attention on the tensor cores (attn_split_sm100.cu) against the oracle.
 
-f32 operands at head_dim 64 and 128 run as bf16 hi/lo planes with three
-UMMAs per product (hi.lo + lo.hi + hi.hi). The representation error of
-hi + lo is at most 2^-16 relative and the dropped lo.lo term at most 2^-16
-of |a||b| (about 1e-5 per product in practice), so results sit far inside the
-f32 path's 1e-3 max-abs bound: the checks here compare with the oracle run in
-f64 at 1e-4 max-abs on N(0,1) inputs, and the f32 SIMT kernel (f32 FMA
-arithmetic) gives the baseline for how close f32 gets. Large scores move the
-error towards the bound (the absolute error of a score grows with its size),
-which test_split_extreme_scores measures.
+f32 operands at head_dim 64 and 128 run as f16 hi/lo planes of the operand
+times a power of two, with three UMMAs per product (hi.lo + lo.hi + hi.hi).
+The representation error of hi + lo is at most 2^-22 relative and the dropped
+lo.lo term at most 2^-22 of |a||b|, the precision of a 3xTF32 split, so
+results sit far inside the f32 path's 1e-3 max-abs bound: the checks here
+compare with the oracle run in f64 at 5e-5 max-abs on N(0,1) inputs, next to
+the f32 SIMT kernel (f32 FMA arithmetic). Large scores move the error towards
+the bound (the absolute error of a score grows with its size), which
+test_split_extreme_scores measures; test_split_stale_running_max holds the
+forward's P planes at the largest value lazy rescaling lets P reach.
 """
 import math
 
@@ -21,7 +22,7 @@ from oracle import oracle as ora
 
 pytestmark = pytest.mark.gpu
 
-TIGHT = 1e-4   # split path vs the f64 oracle
+TIGHT = 5e-5   # split path vs the f64 oracle on N(0,1) inputs
 BOUND = 1e-3   # the f32 path's contract
 
 
@@ -82,6 +83,8 @@ def test_split_close_to_simt_f32(D):
     e_simt = _errs((got_simt[0],) + got_simt[2:], ref)
     print(f"D={D}: split {e_split}  simt {e_simt}")
     assert max(e_split.values()) <= TIGHT and max(e_simt.values()) <= TIGHT
+    # the split path is within a few times the f32 kernel's own rounding
+    assert max(e_split.values()) <= 8 * max(max(e_simt.values()), 1e-6)
 
 
 def test_split_strided_and_unaligned_layouts():
@@ -140,3 +143,25 @@ def test_split_extreme_scores():
     print(f"extreme scores: {err}")
     assert max(err.values()) <= BOUND, err
     assert np.isfinite(lse.cpu().numpy()).all()
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+def test_split_stale_running_max(causal):
+    """Key tiles whose scores step up by 5.5 (7.9 in log2 units, just under
+    the 2^8 lazy-rescale threshold): the forward's P relative to the stale
+    running max reaches ~2^7.9, and its f16 planes must still hold it."""
+    BH, S, D = 2, 256, 128
+    scale = 1.0 / math.sqrt(D)
+    q = np.zeros((BH, S, D), np.float32)
+    q[..., 0] = 1.0
+    k = np.zeros((BH, S, D), np.float32)
+    k[..., 0] = (5.5 * (np.arange(S) // 64) / scale)[None, :]
+    k[..., 1:] = _host((BH, S, D - 1), 11) * 0.01
+    v, do = _host((BH, S, D), 12), _host((BH, S, D), 13)
+    (o, lse, dq, dk, dv), paths = _run(q, k, v, do, scale, causal)
+    assert paths == ("tcgen05", "tcgen05")
+    ro, rlse, rdq, rdk, rdv = ora.attn_rows(q, k, v, do, scale, causal, f64=True)
+    err = _errs((o, dq, dk, dv), (ro, rdq, rdk, rdv))
+    print(f"stale running max: {err}")
+    assert all(np.isfinite(list(err.values())))
+    assert max(err.values()) <= BOUND, err
