@@ -36,7 +36,10 @@
 //               tiles of BQ rows: S^T = K Q^T, dP^T = V dO^T, P^T and
 //               dS^T = P^T (dP^T - delta) as hi | lo in TMEM, dV += P^T dO,
 //               dK += dS^T Q (TS), dQ from an smem dS tile, added into the f32
-//               dQ output by a drain warpgroup (red.global.add).
+//               dQ output by a drain warpgroup (red.global.add). Q and dO
+//               have a stage each, released separately (dO after dV, Q after
+//               dK), and the MMA order lets the next Q load run behind dK and
+//               the next dP^T.
 //
 // Every mbarrier wait is bounded (sm100_ptx.cuh): on expiry the CTA raises an
 // abort flag, records the site in the context's status word, drains its own
@@ -60,6 +63,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 __device__ __forceinline__ uint32_t bar_addr(const uint64_t& b) { return smem_addr(&b); }
+
+// Four consecutive f32 atomic adds in one 16-byte reduction (addr 16-byte aligned).
+__device__ __forceinline__ void red_add_v4_f32(float* addr, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
 
 // Packed f16 pair, round to nearest even; the low half holds `lo`.
 __device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
@@ -134,6 +143,8 @@ struct PreParams {
     float* lse2;          // backward: [B*H][S_pad] lse * log2(e), 0 past S
     float* delta;         // backward: [B*H][S_pad] rowsum(dO * O), 0 past S
     float* dq;            // backward: zeroed, strided like the operands
+    float* dk;            // backward: zeroed (the kernel adds dK segments)
+    float* dv;            // backward: zeroed (the kernel adds dV segments)
     Stats* stats;         // written by split_stats, read by split_pre
     int S_pad;
 };
@@ -234,14 +245,18 @@ __global__ void __launch_bounds__(256) split_pre_kernel(const PreParams p, const
             if (bwd) {
                 const float4 a = load4<VEC>(p.o + off), g = load4<VEC>(p.src[3] + off);
                 acc = fmaf(a.x, g.x, fmaf(a.y, g.y, fmaf(a.z, g.z, a.w * g.w)));
-                float* z = p.dq + off;
-                if (VEC) {
-                    *reinterpret_cast<float4*>(z) = make_float4(0.f, 0.f, 0.f, 0.f);
-                } else {
-                    z[0] = 0.f;
-                    z[1] = 0.f;
-                    z[2] = 0.f;
-                    z[3] = 0.f;
+                float* zs[3] = {p.dq + off, p.dk + off, p.dv + off};
+#pragma unroll
+                for (int zi = 0; zi < 3; ++zi) {
+                    float* z = zs[zi];
+                    if (VEC) {
+                        *reinterpret_cast<float4*>(z) = make_float4(0.f, 0.f, 0.f, 0.f);
+                    } else {
+                        z[0] = 0.f;
+                        z[1] = 0.f;
+                        z[2] = 0.f;
+                        z[3] = 0.f;
+                    }
                 }
             }
         }
@@ -691,6 +706,14 @@ constexpr int kRegsLaunch = 128;
 constexpr int kRegsCtl = 128;
 constexpr int kRegsCompute = 152;
 constexpr int kRegsDrain = 80;
+// dV and dK accumulate in TMEM over segments of at most this many queries,
+// then the drain warpgroup adds the partial sums into the f32 outputs (zeroed
+// by split_pre; RN f32 reductions in L2, fire-and-forget, beside the P/dS work
+// of the next tile) and the next segment starts from zero: the error of the
+// tensor core's long accumulations (which grew with S: dV 2.4e-4 at S = 16384
+// without segments) stays that of a 2048-query sum. Segments of 1024 queries
+// cost 5 % of the backward at C3 (two alternations), 2048 about half that.
+constexpr int kFlushQueries = 2048;
 static_assert(kRegsCtl + 2 * kRegsCompute + kRegsDrain == 4 * kRegsLaunch, "register split");
 
 template <int D>
@@ -700,6 +723,7 @@ struct Cfg {
     // way M = 128 and the accumulator has one row per TMEM lane.
     static constexpr bool DQ_T = D == 128;
     static constexpr int HC = BQ / 2;         // query columns per P/dS warpgroup
+    static constexpr int FLUSH = kFlushQueries / BQ;  // query tiles per dV/dK segment
     static constexpr int CHK = BK * 128;      // 64-column (128-byte) chunk of a K/V plane tile
     static constexpr int CHQ = BQ * 128;      // ... of a Q/dO plane tile
     static constexpr int CHDS = BK * 128;     // ... of a dS plane tile (64 queries wide)
@@ -724,9 +748,12 @@ struct Cfg {
 };
 
 struct Bars {
-    uint64_t kv_full, q_full, q_empty;
+    uint64_t kv_full;
+    uint64_t q_full, q_empty;    // Q hi/lo, lse and delta of a query tile
+    uint64_t do_full, do_empty;  // dO hi/lo of a query tile (released earlier, after dV)
     uint64_t s_full, dp_full, p_full, ds_full;
     uint64_t dsfree;  // smem dS tile read by dQ (-> P/dS warpgroups)
+    uint64_t flush_ready, flush_done;  // dV/dK segment complete (-> drain) / added to the outputs (-> MMA)
     uint64_t dq_full, dq_empty;
     uint64_t acc_done, done;
     uint32_t tmem_base;
@@ -750,6 +777,30 @@ struct Params {
     const Stats* stats;  // plane scales of q, k, v, dout and the dS bound
     DeviceStatus* status;
 };
+
+// dst[0, D) += m * (this lane's D accumulator columns from taddr): TMEM ->
+// registers in 32-column pieces, then f32 reductions (16-byte ones when the
+// row is aligned) that no later instruction waits for.
+template <int D>
+__device__ __forceinline__ void add_rows(uint32_t taddr, float m, float* dst, bool valid, bool vec) {
+#pragma unroll 1
+    for (int c = 0; c < D; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(taddr + c, v);
+        tmem_ld_wait();
+        reg_fence<32>(v);
+        if (!valid) continue;
+        if (vec) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+                red_add_v4_f32(dst + c + i, __uint_as_float(v[i]) * m, __uint_as_float(v[i + 1]) * m,
+                               __uint_as_float(v[i + 2]) * m, __uint_as_float(v[i + 3]) * m);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) red_add_f32(dst + c + i, __uint_as_float(v[i]) * m);
+        }
+    }
+}
 
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -786,11 +837,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(bar_addr(bars->kv_full), 1);
         mbar_init(bar_addr(bars->q_full), 1);
         mbar_init(bar_addr(bars->q_empty), 1);
+        mbar_init(bar_addr(bars->do_full), 1);
+        mbar_init(bar_addr(bars->do_empty), 1);
         mbar_init(bar_addr(bars->s_full), 1);
         mbar_init(bar_addr(bars->dp_full), 1);
         mbar_init(bar_addr(bars->p_full), 256);
         mbar_init(bar_addr(bars->ds_full), 256);
         mbar_init(bar_addr(bars->dsfree), 1);
+        mbar_init(bar_addr(bars->flush_ready), 1);
+        mbar_init(bar_addr(bars->flush_done), 128);
         mbar_init(bar_addr(bars->dq_full), 1);
         mbar_init(bar_addr(bars->dq_empty), 128);
         mbar_init(bar_addr(bars->acc_done), 1);
@@ -836,35 +891,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tma_load_4d(smem_addr(sm + C::V_OFF + pl * C::KT + c * C::CHK), pl ? &tvl : &tvh, kvb, c * 64,
                                 k0, h, b);
                 }
-            int issued = 0;
+            // One stage each: dO(it) once dV(it-1) has read dO(it-1), then Q(it)
+            // with its lse and delta rows once dK(it-1) has read Q(it-1).
+            int nq = 0, ndo = 0;
             for (int it = 0; it < n_it; ++it) {
                 const int q0 = (i_start + it) * BQ;
+                if (!mbar_wait(bar_addr(bars->do_empty), (it & 1) ^ 1, abort_flag, p.status, 141)) break;
+                const uint32_t db = bar_addr(bars->do_full);
+                mbar_arrive_expect_tx(db, 2 * C::QT);
+                for (int pl = 0; pl < 2; ++pl)
+                    for (int c = 0; c < D / 64; ++c)
+                        tma_load_4d(smem_addr(sm + C::DO_OFF + pl * C::QT + c * C::CHQ), pl ? &tdol : &tdoh, db,
+                                    c * 64, q0, h, b);
+                ndo = it + 1;
                 if (!mbar_wait(bar_addr(bars->q_empty), (it & 1) ^ 1, abort_flag, p.status, 140)) break;
                 const uint32_t qb = bar_addr(bars->q_full);
-                mbar_arrive_expect_tx(qb, 4 * C::QT + 2 * BQ * 4);
+                mbar_arrive_expect_tx(qb, 2 * C::QT + 2 * BQ * 4);
                 for (int pl = 0; pl < 2; ++pl)
-                    for (int c = 0; c < D / 64; ++c) {
+                    for (int c = 0; c < D / 64; ++c)
                         tma_load_4d(smem_addr(sm + C::Q_OFF + pl * C::QT + c * C::CHQ), pl ? &tql : &tqh, qb,
                                     c * 64, q0, h, b);
-                        tma_load_4d(smem_addr(sm + C::DO_OFF + pl * C::QT + c * C::CHQ), pl ? &tdol : &tdoh, qb,
-                                    c * 64, q0, h, b);
-                    }
                 const int64_t row0 = bh * p.S_pad + q0;
                 bulk_load(smem_addr(s_lse), p.lse2 + row0, BQ * 4, qb);
                 bulk_load(smem_addr(s_del), p.delta + row0, BQ * 4, qb);
-                issued = it + 1;
+                nq = it + 1;
             }
             mbar_wait_drain(kvb, 0);
-            if (issued > 0) mbar_wait_drain(bar_addr(bars->q_full), (issued - 1) & 1);
+            if (nq > 0) mbar_wait_drain(bar_addr(bars->q_full), (nq - 1) & 1);
+            if (ndo > 0) mbar_wait_drain(bar_addr(bars->do_full), (ndo - 1) & 1);
         }
         __syncwarp();
         tc_fence_before();
         __syncthreads();
     } else if (warp < 4) {
         // ------------------------------------------------------------ MMA issuer (warp 1, lane 0)
-        // Per query tile: S^T, dP^T (the P/dS warpgroups work on S^T while
-        // dP^T runs), dV once P^T is in TMEM, dK once dS^T is, then dQ. Each
-        // product is hi.lo + lo.hi + hi.hi over the two planes.
+        // Order: S^T(0), dP^T(0); then per query tile it: dV(it) once P^T is in
+        // TMEM (releases dO), dK(it) once dS^T is (releases Q), dP^T(it+1),
+        // S^T(it+1), dQ(it). The reload of Q(it+1) runs behind dK(it) and
+        // dP^T(it+1), and dQ(it) behind the P phase of tile it+1. Each product
+        // is hi.lo + lo.hi + hi.hi over the two planes.
         if (warp == 1 && lane == 0) {
             constexpr uint32_t idSP = idesc_f16(BK, BQ, false, false);
             constexpr uint32_t idAcc = idesc_f16(BK, D, false, true);
@@ -906,25 +971,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                     umma_ts(d, ah, desc_of(bb + mnmaj(kk), hi), idAcc, 1u);
                 }
             };
-            bool ok = mbar_wait(bar_addr(bars->kv_full), 0, abort_flag, p.status, 150);
-            for (int it = 0; ok && it < n_it; ++it) {
-                const bool first = it == 0;
-                if (!(ok = mbar_wait(bar_addr(bars->q_full), it & 1, abort_flag, p.status, 151))) break;
+            // S^T = K Q^T overwrites P^T(it-1), which dV(it-1), issued earlier by
+            // this thread, has read; dP^T = V dO^T likewise after dK(it-1).
+            auto issue_S = [&](int it) {
+                if (!mbar_wait(bar_addr(bars->q_full), it & 1, abort_flag, p.status, 151)) return false;
                 tc_fence_after();
-                // S^T = K Q^T, dP^T = V dO^T (S^T overwrites P^T(it-1), which dV(it-1),
-                // issued earlier by this thread, has read; likewise dP^T and dK).
                 kk3(tmem + C::C_S, kK, pK, C::CHK, kQ, pQ, C::CHQ, NS, idSP);
                 umma_commit(bar_addr(bars->s_full));
+                return true;
+            };
+            auto issue_DP = [&](int it) {
+                if (!mbar_wait(bar_addr(bars->do_full), it & 1, abort_flag, p.status, 156)) return false;
+                tc_fence_after();
                 kk3(tmem + C::C_DP, kV, pK, C::CHK, kDO, pQ, C::CHQ, NS, idSP);
                 umma_commit(bar_addr(bars->dp_full));
+                return true;
+            };
+            bool ok = mbar_wait(bar_addr(bars->kv_full), 0, abort_flag, p.status, 150);
+            if (ok && n_it > 0) ok = issue_S(0) && issue_DP(0);
+            for (int it = 0; ok && it < n_it; ++it) {
+                // A new dV/dK segment starts from zero once the last one is in the outputs.
+                const bool first = (it % C::FLUSH) == 0;
+                if (first && it > 0 &&
+                    !(ok = mbar_wait(bar_addr(bars->flush_done), (it / C::FLUSH - 1) & 1, abort_flag, p.status,
+                                     157)))
+                    break;
                 if (!(ok = mbar_wait(bar_addr(bars->p_full), it & 1, abort_flag, p.status, 152))) break;
                 tc_fence_after();
                 ts3(tmem + C::C_DV, C::C_S, mDO, pQ, first);  // dV += P^T dO
+                umma_commit(bar_addr(bars->do_empty));        // dO(it) is read by nothing after dV(it)
                 if (!(ok = mbar_wait(bar_addr(bars->ds_full), it & 1, abort_flag, p.status, 154))) break;
                 tc_fence_after();
                 ts3(tmem + C::C_DK, C::C_DP, mQ, pQ, first);  // dK += dS^T Q
-                // Q(it), dO(it), lse and delta are read by nothing after dK(it).
+                // Q(it), lse and delta are read by nothing after dK(it).
                 umma_commit(bar_addr(bars->q_empty));
+                if (it % C::FLUSH == C::FLUSH - 1 && it + 1 < n_it) umma_commit(bar_addr(bars->flush_ready));
+                if (it + 1 < n_it && !(ok = issue_DP(it + 1) && issue_S(it + 1))) break;
                 if (!(ok = mbar_wait(bar_addr(bars->dq_empty), (it & 1) ^ 1, abort_flag, p.status, 155))) break;
                 tc_fence_after();
                 const uint32_t dq = tmem + C::C_DQ;
@@ -968,6 +1050,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sl2 = p.scale * kLog2e / (sk * sq);
         const float dpu = 1.f / (sv * sdo);
         const int c0 = g * HC;
+        // Warpgroup 0 owns dV, warpgroup 1 dK (times scale): this thread's key
+        // row of the accumulator, stored by the first add and added to after.
+        const uint32_t acc_col = g ? C::C_DK : C::C_DV;
+        const float acc_mul = g ? p.scale / (sds * sq) : 1.f / (kPScaleBwd * sdo);
+        float* acc_dst = (g ? p.dk : p.dv) + (int64_t)b * p.sb + (int64_t)h * p.sh + (int64_t)kr * p.ss;
+        // The last segment is added like the earlier ones (drain warpgroup).
+        auto flush = [&]() { add_rows<D>(tl + acc_col, acc_mul, acc_dst, kr < p.S, p.vec != 0); };
         bool ok = true;
         for (int it = 0; it < n_it; ++it) {
             const int q0 = (i_start + it) * BQ;
@@ -1057,33 +1146,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             mbar_arrive(bar_addr(bars->ds_full));
         }
-        // Epilogue: warpgroup 0 stores dV, warpgroup 1 stores dK (times scale).
+        // Epilogue: the last segment of dV / dK.
         if (ok && mbar_wait(bar_addr(bars->acc_done), 0, abort_flag, p.status, 163)) {
             tc_fence_after();
-            const bool store = kr < p.S;
-            const uint32_t col = g ? C::C_DK : C::C_DV;
-            const float mul = g ? p.scale / (sds * sq) : 1.f / (kPScaleBwd * sdo);
-            float* dst = (g ? p.dk : p.dv) + (int64_t)b * p.sb + (int64_t)h * p.sh + (int64_t)kr * p.ss;
-#pragma unroll
-            for (int c = 0; c < D; c += 32) {
-                uint32_t v[32];
-                tmem_ld32(tl + col + c, v);
-                tmem_ld_wait();
-                reg_fence<32>(v);
-                if (store) {
-                    if (p.vec) {
-                        float4* d4 = reinterpret_cast<float4*>(dst + c);
-#pragma unroll
-                        for (int q4 = 0; q4 < 8; ++q4)
-                            d4[q4] = make_float4(__uint_as_float(v[4 * q4]) * mul, __uint_as_float(v[4 * q4 + 1]) * mul,
-                                                 __uint_as_float(v[4 * q4 + 2]) * mul,
-                                                 __uint_as_float(v[4 * q4 + 3]) * mul);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) dst[c + i] = __uint_as_float(v[i]) * mul;
-                    }
-                }
-            }
+            flush();
         }
         tc_fence_before();
         __syncthreads();
@@ -1098,8 +1164,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
         float* base = p.dq + (int64_t)b * p.sb + (int64_t)h * p.sh;
         const float mul = p.scale / (ds_scale(p.stats) * pow2_scale(p.stats->maxabs[1]));  // dQ = scale dS K
+        // Segment flushes: lane r holds key row k0 + r of the dV and dK accumulators.
+        const int kr = k0 + r;
+        const float mul_dv = 1.f / (kPScaleBwd * pow2_scale(p.stats->maxabs[3]));
+        const float mul_dk = p.scale / (ds_scale(p.stats) * pow2_scale(p.stats->maxabs[0]));
+        const int64_t row_off = (int64_t)b * p.sb + (int64_t)h * p.sh + (int64_t)kr * p.ss;
+
         for (int it = 0; it < n_it; ++it) {
             const int q0 = (i_start + it) * BQ;
+            if (it % C::FLUSH == C::FLUSH - 1 && it + 1 < n_it) {  // a dV/dK segment is complete
+                if (!mbar_wait(bar_addr(bars->flush_ready), (it / C::FLUSH) & 1, abort_flag, p.status, 165)) break;
+                tc_fence_after();
+                add_rows<D>(tl + C::C_DV, mul_dv, p.dv + row_off, kr < p.S, p.vec != 0);
+                add_rows<D>(tl + C::C_DK, mul_dk, p.dk + row_off, kr < p.S, p.vec != 0);
+                tc_fence_before();
+                mbar_arrive(bar_addr(bars->flush_done));
+            }
             if (!mbar_wait(bar_addr(bars->dq_full), it & 1, abort_flag, p.status, 170)) break;
             tc_fence_after();
             uint32_t v[C::DQ_COLS];
@@ -1116,10 +1196,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = 0; c < BQ; ++c)
                     if (c < nq) red_add_f32(dst + (int64_t)c * p.ss, __uint_as_float(v[c]) * mul);
             } else {
-                if (q0 + r < p.S) {
+                if (q0 + r < p.S) {  // one query row per thread: 16-byte vector adds when aligned
                     float* dst = base + (int64_t)(q0 + r) * p.ss;
+                    if (p.vec) {
 #pragma unroll
-                    for (int c = 0; c < D; ++c) red_add_f32(dst + c, __uint_as_float(v[c]) * mul);
+                        for (int c = 0; c < D; c += 4)
+                            red_add_v4_f32(dst + c, __uint_as_float(v[c]) * mul, __uint_as_float(v[c + 1]) * mul,
+                                           __uint_as_float(v[c + 2]) * mul, __uint_as_float(v[c + 3]) * mul);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < D; ++c) red_add_f32(dst + c, __uint_as_float(v[c]) * mul);
+                    }
                 }
             }
         }
@@ -1281,6 +1368,8 @@ cudaError_t launch_bwd(cudaStream_t st, int sm_count, DeviceStatus* status, cons
     pp.lse2 = (float*)tail;
     pp.delta = (float*)(tail + table_bytes(d));
     pp.dq = dq;
+    pp.dk = dk;
+    pp.dv = dv;
     pp.S_pad = s_pad_of(d);
     const bool vec = vec_ok(d, {q, k, v, o, dout, dq, dk, dv});
     cudaError_t e = launch_pre<D>(st, sm_count, pp, d, vec);

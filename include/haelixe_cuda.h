@@ -391,7 +391,9 @@ int hx_group_sync(hx_group* group, int member);
 /* Number of kernels this context has launched so far. */
 uint64_t hx_kernel_launches(const hx_ctx* ctx);
 /* Which kernel family the last attention call used on this context:
- * 0 none, 1 SIMT (f32 / any head_dim), 2 tcgen05 (bf16, head_dim 64 or 128). */
+ * 0 none, 1 SIMT (any other head_dim, or forced), 2 tcgen05 (head_dim 64 or
+ * 128: bf16 directly, f32 as f16 hi/lo operand planes with three MMAs per
+ * product and a workspace from the context's arena in the forward). */
 int hx_last_path(const hx_ctx* ctx);
 /* Forces the SIMT kernels (1) or restores automatic selection (0). */
 int hx_set_force_simt(hx_ctx* ctx, int force);

@@ -87,11 +87,15 @@ def test_split_close_to_simt_f32(D):
     assert max(e_split.values()) <= 8 * max(max(e_simt.values()), 1e-6)
 
 
-def test_split_strided_and_unaligned_layouts():
+@pytest.mark.parametrize("D,S", [(64, 333), (128, 2200)])
+def test_split_strided_and_unaligned_layouts(D, S):
     """[B,S,H,D] views (float4 path) and rows at an odd element offset (scalar
     path) give the contiguous call's forward bit for bit (the forward has no
-    atomics) and its gradients to rounding (dQ is added with atomics)."""
-    B, S, H, D = 2, 333, 3, 64
+    atomics) and its gradients to rounding (dQ, dK and dV are added with
+    atomics). At D=128, S=2200 the dV/dK accumulation of the first key tiles
+    runs in two segments (2048 queries each at most), so both paths add more
+    than one segment into the outputs."""
+    B, H = 2, 3
     base = [torch.from_numpy(_host((B, S, H, D), 70 + i)).cuda() for i in range(4)]
     views = [t.permute(0, 2, 1, 3) for t in base]
     wide = [torch.zeros(B, H, S, D + 1, device="cuda") for _ in range(4)]
