@@ -21,10 +21,12 @@
 //
 // Scales: Q, K, V, dO per tensor from their max-abs (split_stats); P by 2^14
 // in the backward (P <= 1) and 2^6 in the forward (P <= 2^8 under lazy
-// rescaling); dS by the bound |dS| <= |dP| + |delta| <= 2 max|dO_q|
-// max|V_k| (row 2-norms; O is a convex combination of V rows).
+// rescaling); dS by the bound |dS| <= |dP| + |delta| <= 2 D max|dO| max|V|
+// (O is a convex combination of V rows). Elements far below a bound keep an
+// absolute error under 2^-39 of it, so a loose bound costs no precision that
+// matters.
 //
-//   split_stats max-abs and largest row 2-norm of each f32 operand.
+//   split_stats max-abs of each f32 operand.
 //   split_pre   f32 Q, K, V (and dO) -> contiguous f16 hi/lo planes
 //               [B*H][S][D]; in the backward also lse * log2(e),
 //               delta = rowsum(dO * O) in f32, and dQ := 0.
@@ -49,6 +51,7 @@
 
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <initializer_list>
 
 #include "sm100_ptx.cuh"
@@ -116,15 +119,15 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn_major, 
 }
 
 // Operand statistics (device, zeroed before split_stats): f32 bits of the
-// max-abs and of the largest row 2-norm squared of q, k, v, dout.
+// max-abs of q, k, v, dout.
 struct Stats {
     uint32_t maxabs[4];
-    uint32_t maxn2[4];
 };
 
-// Scale of the dS planes from the bound |dS| <= 2 max|dO_q| max|V_k|.
+// Scale of the dS planes from the bound |dS| <= 2 D max|dO| max|V|.
+template <int D>
 __device__ __forceinline__ float ds_scale(const Stats* st) {
-    const float b = 2.f * sqrtf(__uint_as_float(st->maxn2[3])) * sqrtf(__uint_as_float(st->maxn2[2]));
+    const float b = 2.f * (float)D * __uint_as_float(st->maxabs[3]) * __uint_as_float(st->maxabs[2]);
     return pow2_scale(__float_as_uint(b));
 }
 
@@ -155,10 +158,12 @@ __device__ __forceinline__ float4 load4(const float* p) {
     return make_float4(p[0], p[1], p[2], p[3]);
 }
 
-// Max-abs and largest row 2-norm squared of each operand: D/4 lanes per row
-// (one float4 each), grid-stride over the rows [B*H][S]; per-thread running
-// maxima, one atomicMax per warp and operand at the end (non-negative f32
-// values order like their bits).
+// Max-abs of each operand: D/4 lanes per row (one float4 each), grid-stride
+// over the rows [B*H][S], two rows per lane group per iteration; per-thread
+// running maxima (no cross-lane work in the loop), reduced over the block and
+// added with one atomicMax per block and operand (non-negative f32 values
+// order like their bits). The grid is four blocks per SM: one atomic per warp
+// on the same four words had made this pass twice as slow as the split.
 template <int D, bool VEC>
 __global__ void __launch_bounds__(256) split_stats_kernel(const PreParams p, const AttnDims d) {
     constexpr int G = D / 4;
@@ -166,43 +171,41 @@ __global__ void __launch_bounds__(256) split_stats_kernel(const PreParams p, con
     const int64_t rows = (int64_t)d.B * d.H * d.S;
     const int lane = threadIdx.x % 32, sub = lane % G;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x / 32);
-    float mabs[4] = {0.f, 0.f, 0.f, 0.f}, mn2[4] = {0.f, 0.f, 0.f, 0.f};
+    float mabs[4] = {0.f, 0.f, 0.f, 0.f};
     for (int64_t r0 = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * RPW; r0 < rows;
-         r0 += nwarps * RPW) {
-        const int64_t r = r0 + lane / G;
-        const bool row_ok = r < rows;
-        const int64_t bhi = row_ok ? r / d.S : 0;
-        const int s = row_ok ? (int)(r % d.S) : 0;
-        const int64_t off = (bhi / d.H) * d.sb + (bhi % d.H) * d.sh + (int64_t)s * d.ss + sub * 4;
+         r0 += 2 * nwarps * RPW) {
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            if (t < p.n) {
-                float n2 = 0.f;
-                if (row_ok) {
+        for (int u = 0; u < 2; ++u) {
+            const int64_t r = r0 + u * nwarps * RPW + lane / G;
+            if (r >= rows) continue;
+            // rows < 2^32 (checked on the host): 32-bit divisions
+            const uint32_t bhi = (uint32_t)r / (uint32_t)d.S;
+            const uint32_t s = (uint32_t)r - bhi * (uint32_t)d.S;
+            const uint32_t bb = bhi / (uint32_t)d.H, hh = bhi - bb * (uint32_t)d.H;
+            const int64_t off = (int64_t)bb * d.sb + (int64_t)hh * d.sh + (int64_t)s * d.ss + sub * 4;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                if (t < p.n) {
                     const float4 x = load4<VEC>(p.src[t] + off);
                     mabs[t] = fmaxf(mabs[t], fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
-                    n2 = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
                 }
-#pragma unroll
-                for (int w = G / 2; w > 0; w >>= 1) n2 += __shfl_xor_sync(0xffffffffu, n2, w);
-                mn2[t] = fmaxf(mn2[t], n2);
             }
         }
     }
+    __shared__ float red[8][4];  // [warp][operand]; 256 threads
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
-        if (t < p.n) {
-            float a = mabs[t], n2 = mn2[t];
+        float a = mabs[t];
 #pragma unroll
-            for (int w = 16; w > 0; w >>= 1) {
-                a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, w));
-                n2 = fmaxf(n2, __shfl_xor_sync(0xffffffffu, n2, w));
-            }
-            if (lane == 0) {
-                atomicMax(&p.stats->maxabs[t], __float_as_uint(a));
-                atomicMax(&p.stats->maxn2[t], __float_as_uint(n2));
-            }
-        }
+        for (int w = 16; w > 0; w >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, w));
+        if (lane == 0) red[threadIdx.x / 32][t] = a;
+    }
+    __syncthreads();
+    if (threadIdx.x < (unsigned)p.n) {
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) a = fmaxf(a, red[w][threadIdx.x]);
+        atomicMax(&p.stats->maxabs[threadIdx.x], __float_as_uint(a));
     }
 }
 
@@ -223,14 +226,15 @@ __global__ void __launch_bounds__(256) split_pre_kernel(const PreParams p, const
          r0 += nwarps * RPW) {
         const int64_t r = r0 + lane / G;
         const bool row_ok = r < rows;
-        const int s = row_ok ? (int)(r % p.S_pad) : 0;
-        const int64_t bhi = row_ok ? r / p.S_pad : 0;
+        // rows < 2^32 (checked on the host): 32-bit divisions
+        const uint32_t bhi = row_ok ? (uint32_t)r / (uint32_t)p.S_pad : 0u;
+        const int s = row_ok ? (int)((uint32_t)r - bhi * (uint32_t)p.S_pad) : 0;
         const bool in_seq = row_ok && s < d.S;
         float acc = 0.f;
         if (in_seq) {
-            const int hh = (int)(bhi % d.H), bb = (int)(bhi / d.H);
+            const uint32_t bb = bhi / (uint32_t)d.H, hh = bhi - bb * (uint32_t)d.H;
             const int64_t off = (int64_t)bb * d.sb + (int64_t)hh * d.sh + (int64_t)s * d.ss + sub * 4;
-            const int64_t poff = (bhi * d.S + s) * D + sub * 4;
+            const int64_t poff = ((int64_t)bhi * d.S + s) * D + sub * 4;
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
                 if (t < p.n) {
@@ -265,7 +269,7 @@ __global__ void __launch_bounds__(256) split_pre_kernel(const PreParams p, const
             for (int w = G / 2; w > 0; w >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, w);
             if (row_ok && sub == 0) {
                 p.delta[r] = in_seq ? acc : 0.f;
-                p.lse2[r] = in_seq ? p.lse[bhi * d.S + s] * kLog2e : 0.f;
+                p.lse2[r] = in_seq ? p.lse[(int64_t)bhi * d.S + s] * kLog2e : 0.f;
             }
         }
     }
@@ -1046,7 +1050,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // go in scaled by kPScaleBwd and sds (powers of two: exact).
         const float sq = pow2_scale(p.stats->maxabs[0]), sk = pow2_scale(p.stats->maxabs[1]),
                     sv = pow2_scale(p.stats->maxabs[2]), sdo = pow2_scale(p.stats->maxabs[3]);
-        const float sds = ds_scale(p.stats);
+        const float sds = ds_scale<D>(p.stats);
         const float sl2 = p.scale * kLog2e / (sk * sq);
         const float dpu = 1.f / (sv * sdo);
         const int c0 = g * HC;
@@ -1163,11 +1167,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = wi * 32 + lane;
         const uint32_t tl = tmem + ((uint32_t)(wi * 32) << 16);
         float* base = p.dq + (int64_t)b * p.sb + (int64_t)h * p.sh;
-        const float mul = p.scale / (ds_scale(p.stats) * pow2_scale(p.stats->maxabs[1]));  // dQ = scale dS K
+        const float mul = p.scale / (ds_scale<D>(p.stats) * pow2_scale(p.stats->maxabs[1]));  // dQ = scale dS K
         // Segment flushes: lane r holds key row k0 + r of the dV and dK accumulators.
         const int kr = k0 + r;
         const float mul_dv = 1.f / (kPScaleBwd * pow2_scale(p.stats->maxabs[3]));
-        const float mul_dk = p.scale / (ds_scale(p.stats) * pow2_scale(p.stats->maxabs[0]));
+        const float mul_dk = p.scale / (ds_scale<D>(p.stats) * pow2_scale(p.stats->maxabs[0]));
         const int64_t row_off = (int64_t)b * p.sb + (int64_t)h * p.sh + (int64_t)kr * p.ss;
 
         for (int it = 0; it < n_it; ++it) {
@@ -1267,9 +1271,10 @@ int64_t pre_blocks(int64_t rows, int D, int sm_count) {
 // Zeroes the Stats block, gathers the operand statistics, then writes the planes.
 template <int D>
 cudaError_t launch_pre(cudaStream_t st, int sm_count, const PreParams& pp, const AttnDims& d, bool vec) {
+    if ((uint64_t)d.B * d.H * pp.S_pad >= (1ull << 32)) return cudaErrorInvalidConfiguration;  // 32-bit row index
     cudaError_t e = cudaMemsetAsync(pp.stats, 0, sizeof(Stats), st);
     if (e != cudaSuccess) return e;
-    const int64_t sb = pre_blocks((int64_t)d.B * d.H * d.S, D, sm_count);
+    const int64_t sb = std::min<int64_t>(pre_blocks((int64_t)d.B * d.H * d.S, D, sm_count), 4 * (int64_t)sm_count);
     if (vec)
         split_stats_kernel<D, true><<<(unsigned)sb, 256, 0, st>>>(pp, d);
     else
