@@ -316,7 +316,6 @@ struct Bars {
     uint64_t q_full;
     uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
     uint64_t s_full[NWG], p_full[NWG], o_full[NWG];
-    uint64_t p_half[NWG];  // P of the tile's first BN/2 keys is in TMEM
     uint64_t turn[NWG];    // ping-pong token between the softmax warpgroups
     uint64_t done;
     uint32_t tmem_base;
@@ -383,7 +382,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int w = 0; w < NWG; ++w) {
             mbar_init(bar_addr(bars->s_full[w]), 1);
             mbar_init(bar_addr(bars->p_full[w]), BM);
-            mbar_init(bar_addr(bars->p_half[w]), BM);
             mbar_init(bar_addr(bars->o_full[w]), 1);
             mbar_init(bar_addr(bars->turn[w]), BM);
         }
@@ -522,13 +520,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bool k_next = false;
                 for (int w = 0; w < NWG && ok; ++w) {
                     if (j < n_w[w]) {
-                        if (!(ok = mbar_wait(bar_addr(bars->p_half[w]), j & 1, abort_flag, p.status, 125)))
-                            break;
-                        tc_fence_after();
-                        issue_PV(w, sv, j, 0);
+                        // P is published once per tile: with 64-key tiles two
+                        // hand-offs per tile cost more than the early half won
+                        // (forward 3.93-3.95 -> 3.76-3.81 ms at D=64, -1.5 % at D=128).
                         if (!(ok = mbar_wait(bar_addr(bars->p_full[w]), j & 1, abort_flag, p.status, 123)))
                             break;
                         tc_fence_after();
+                        issue_PV(w, sv, j, 0);
                         issue_PV(w, sv, j, 1);
                     }
                     if (jn < n_w[w]) {
@@ -648,11 +646,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tmem_st16(tS + c / 2, ph);
                 tmem_st16(tS + BN / 2 + c / 2, pl);
-                if (c == BN / 2 - 32) {  // keys [0, BN/2) done: publish the first half of P
-                    tmem_st_wait();
-                    tc_fence_before();
-                    mbar_arrive(bar_addr(bars->p_half[w]));
-                }
             }
             float s0, s1;
             f2_unpack(f2_add(sum_a, sum_b), s0, s1);
