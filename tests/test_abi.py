@@ -76,6 +76,25 @@ def test_workspace_size():
     assert L.hx_attn_bwd_workspace_size(N.HX_F32, ctypes.byref(bad), ctypes.byref(out)) == N.HX_ERR_INVALID
 
 
+def test_workspace_size_covers_the_f32_split_path():
+    """f32 at head_dim 64/128 runs on f16 hi/lo planes: the backward workspace
+    holds a 256-byte statistics block, the hi and lo planes of Q, K, V and dO
+    (2 bytes per element each, 256-byte aligned) and the lse / delta tables
+    over S padded to 128."""
+    L = N.lib()
+    out = ctypes.c_uint64()
+
+    def a256(x):
+        return (x + 255) // 256 * 256
+
+    for B, H, S, D in ((2, 3, 100, 64), (1, 4, 1000, 128)):
+        shp = N.AttnShape(B, H, S, D, H * S * D, S * D, D)
+        assert L.hx_attn_bwd_workspace_size(N.HX_F32, ctypes.byref(shp), ctypes.byref(out)) == 0
+        s_pad = (S + 127) // 128 * 128
+        need = 256 + 8 * a256(B * H * S * D * 2) + 2 * a256(B * H * s_pad * 4)
+        assert out.value >= need, (out.value, need)
+
+
 def test_rust_binding_declares_every_entry_point():
     """The Rust `extern "C"` block of the integration guide binds every function the header declares."""
     import re
