@@ -424,11 +424,17 @@ int hx_attn_fwd_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, cons
     NvtxRange nv("hx_attn_fwd_strided");
     LaunchCount lc(c);
     const hx::AttnDims d = hx::dims_of(*shape);
-    const bool fast = !c->force_simt && lse != nullptr && hx::sm100_supported(dt, d) &&
-                      tma_layout_ok(d, {q, k, v, o});
-    // f32 at head_dim 64/128: tcgen05 on bf16 hi/lo operand planes (a
+    const bool fast = !c->force_simt && hx::sm100_supported(dt, d) && tma_layout_ok(d, {q, k, v, o});
+    // f32 at head_dim 64/128: tcgen05 on f16 hi/lo operand planes (a
     // workspace from the context's arena, released stream-ordered).
-    const bool split = !c->force_simt && lse != nullptr && !fast && hx::split_supported(dt, d);
+    const bool split = !c->force_simt && !fast && hx::split_supported(dt, d);
+    // The tcgen05 kernels always write the log-sum-exp: without a caller
+    // buffer (no backward follows) they get a temporary one from the arena.
+    float* lse_tmp = nullptr;
+    if ((fast || split) && lse == nullptr) {
+        if ((st = hx_alloc(c, (uint64_t)d.B * d.H * d.S * sizeof(float), (void**)&lse_tmp))) return st;
+        lse = lse_tmp;
+    }
     cudaError_t e;
     if (fast) {
         e = hx::sm100_attn_fwd(c->stream, c->sm_count, c->status, d, q, k, v, o, lse, scale,
@@ -436,7 +442,10 @@ int hx_attn_fwd_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, cons
         c->last_path = 2;
     } else if (split) {
         void* ws = nullptr;
-        if ((st = hx_alloc(c, hx::split_fwd_workspace_bytes(d), &ws))) return st;
+        if ((st = hx_alloc(c, hx::split_fwd_workspace_bytes(d), &ws))) {
+            if (lse_tmp) hx_free(c, lse_tmp);
+            return st;
+        }
         e = hx::split_attn_fwd(c->stream, c->sm_count, c->status, d, q, k, v, o, lse, scale, causal, ws);
         hx_free(c, ws);
         c->last_path = 2;
@@ -444,6 +453,7 @@ int hx_attn_fwd_strided(hx_ctx* c, hx_dtype dt, const hx_attn_shape* shape, cons
         e = hx::simt_attn_fwd(c->stream, dt, d, q, k, v, o, lse, scale, causal);
         c->last_path = 1;
     }
+    if (lse_tmp) hx_free(c, lse_tmp);  // stream-ordered: the next user of the slab queues behind us
     return check_cuda(c, e, fast ? "attention forward (tcgen05)"
                                  : split ? "attention forward (tcgen05, split f32)" : "attention forward (SIMT)");
 }

@@ -151,7 +151,8 @@ int hx_host_free_pinned(void* ptr);
 
 /* ---- fused attention, contiguous [BH, S, D] (the reference's layout) -------- */
 /* o = softmax(scale * q k^T [+ causal mask]) v ; lse[BH*S] (f32, may be NULL
- * only when no backward follows) receives the per-row log-sum-exp.
+ * only when no backward follows) receives the per-row log-sum-exp. Without it
+ * the tcgen05 kernels write a temporary one from the context's arena.
  * Mirrors the reference's Params{bh, seq_len, head_dim, scale}
  * (src/gpu/mod.rs:1354) plus the causal flag the reference lacks. */
 int hx_flash_attention_fwd(hx_ctx* ctx, hx_dtype dtype, const void* q, const void* k,

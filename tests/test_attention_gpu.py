@@ -213,6 +213,26 @@ def test_misaligned_operands_take_a_correct_path():
     _check("O", o, ro, torch.bfloat16)
 
 
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float32, 64)], ids=["bf16", "f32"])
+def test_forward_without_lse_stays_on_tcgen05(dtype, D):
+    """hx_attn_fwd_strided with lse = NULL (no backward follows): the tcgen05
+    kernels take a temporary lse from the arena, so an inference call keeps the
+    tensor-core path and gives the same O as the call with an lse buffer."""
+    BH, S = 2, 300
+    q, k, v = (_dev(_host((BH, S, D), 140 + i, dtype), dtype) for i in range(3))
+    ctx = hx.context()
+    o_ref, _ = hx.attn_forward(q, k, v, 0.1, True)
+    o = torch.empty_like(q)
+    shp = hx.attention._shape_of(q)
+    code = N.HX_BF16 if dtype == torch.bfloat16 else N.HX_F32
+    N.check(N.lib().hx_attn_fwd_strided(ctx.handle, code, ctypes.byref(shp), ctypes.c_void_p(q.data_ptr()),
+                                        ctypes.c_void_p(k.data_ptr()), ctypes.c_void_p(v.data_ptr()),
+                                        ctypes.c_void_p(o.data_ptr()), None, 0.1, 1), ctx.handle)
+    assert ctx.last_path == "tcgen05"
+    torch.cuda.synchronize()
+    assert torch.equal(o, o_ref)
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
 @pytest.mark.parametrize("layout", ["bshd", "bhsd"])
 def test_reassemble_heads_kernel(dtype, layout):
