@@ -29,7 +29,7 @@
 //   split_stats max-abs of each f32 operand.
 //   split_pre   f32 Q, K, V (and dO) -> contiguous f16 hi/lo planes
 //               [B*H][S][D]; in the backward also lse * log2(e),
-//               delta = rowsum(dO * O) in f32, and dQ := 0.
+//               delta = rowsum(dO * O) in f32, and dQ, dK, dV := 0.
 //   fwd         two 128-row query tiles per CTA, K/V rings of BN-key tiles:
 //               S = Q K^T (SS), P = exp2(S*scale*log2e - m) written back over
 //               S as packed hi | lo f16, O += P V (TS, P from TMEM); online
@@ -41,7 +41,8 @@
 //               dQ output by a drain warpgroup (red.global.add). Q and dO
 //               have a stage each, released separately (dO after dV, Q after
 //               dK), and the MMA order lets the next Q load run behind dK and
-//               the next dP^T.
+//               the next dP^T. dV and dK accumulate in TMEM over segments of
+//               2048 queries, each added into the f32 outputs.
 //
 // Every mbarrier wait is bounded (sm100_ptx.cuh): on expiry the CTA raises an
 // abort flag, records the site in the context's status word, drains its own
@@ -1047,8 +1048,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sl2 = p.scale * kLog2e / (sk * sq);
         const float dpu = 1.f / (sv * sdo);
         const int c0 = g * HC;
-        // Warpgroup 0 owns dV, warpgroup 1 dK (times scale): this thread's key
-        // row of the accumulator, stored by the first add and added to after.
+        // Warpgroup 0 adds the last segment of dV, warpgroup 1 that of dK
+        // (times scale): this thread's key row, into the zeroed outputs.
         const uint32_t acc_col = g ? C::C_DK : C::C_DV;
         const float acc_mul = g ? p.scale / (sds * sq) : 1.f / (kPScaleBwd * sdo);
         float* acc_dst = (g ? p.dk : p.dv) + (int64_t)b * p.sb + (int64_t)h * p.sh + (int64_t)kr * p.ss;
