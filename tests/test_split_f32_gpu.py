@@ -169,3 +169,21 @@ def test_split_stale_running_max(causal):
     print(f"stale running max: {err}")
     assert all(np.isfinite(list(err.values())))
     assert max(err.values()) <= BOUND, err
+
+
+@pytest.mark.parametrize("S,D,causal", [(16384, 128, True), (8192, 64, False)], ids=["S16384-D128-causal",
+                                                                                   "S8192-D64-full"])
+def test_split_full_length_slices(S, D, causal):
+    """Whole long slices against the f64 oracle: the first key tiles of S=16384
+    accumulate dV and dK over eight 2048-query segments, and the error stays at
+    the short-sequence level (without segments dV reached 2.4e-4 here)."""
+    BH = 1
+    q, k, v, do = (_host((BH, S, D), 500 + D + i) for i in range(4))
+    scale = 1.0 / math.sqrt(D)
+    (o, lse, dq, dk, dv), paths = _run(q, k, v, do, scale, causal)
+    assert paths == ("tcgen05", "tcgen05")
+    ro, rlse, rdq, rdk, rdv = ora.attn_rows(q, k, v, do, scale, causal, f64=True)
+    err = _errs((o, dq, dk, dv), (ro, rdq, rdk, rdv))
+    print(f"S={S} D={D} causal={causal}: max-abs vs f64 oracle {err}")
+    assert max(err.values()) <= 1e-4, err
+    assert np.max(np.abs(lse.cpu().numpy().reshape(rlse.shape) - rlse)) <= TIGHT
