@@ -59,6 +59,11 @@ def _bands_intact(buf, n):
     (torch.bfloat16, 3, 129, 64, False, None),
     (torch.bfloat16, 2, 257, 128, True, 10000.0),
     (torch.float32, 2, 65, 80, True, None),
+    # f32 on the tensor cores (f16 hi/lo planes); S=2200 at D=128 adds the
+    # dV/dK accumulation into the outputs in two segments
+    (torch.float32, 2, 300, 128, True, None),
+    (torch.float32, 3, 129, 64, True, None),
+    (torch.float32, 2, 2200, 128, False, 10000.0),
 ])
 def test_kernels_write_only_their_outputs(dtype, BH, S, D, causal, rope):
     shape = (BH, S, D)
